@@ -1,0 +1,168 @@
+/*
+ * sp24.h — C ABI of the B200 (sm_100a) 2:4 structured-sparse GEMM library.
+ *
+ *   C[M x N] (fp32 accumulate) = A[M x K] * B[K x N]
+ *
+ * A is 2:4-sparse along K and is passed compressed: A_c holds the two kept
+ * values of every aligned group of four (M x K/2, row-major) and the metadata
+ * holds one 4-bit code per group (i0 | i1 << 2, i0 < i1).  B is dense, K x N,
+ * row-major.  Element types: fp16, bf16, fp8 e4m3 (A and B share the type).
+ *
+ * Every entry point is stream-ordered, never exits the process and reports
+ * errors through sp24_status.  Pointers are device pointers unless a comment
+ * says otherwise.  No torch or C++ types cross this boundary.
+ *
+ * Reference interfaces each entry point replaces (paths inside
+ * codes1gn/sparse-gemm-with-hopper-sptc):
+ *   sp24_gemm            wgmma_sp_raw_common.hpp:955-1030 (wgmma_sp_raw_kernel,
+ *                        launched at :1078-1080) and the CuTe twin
+ *                        wgmma_sp_demo_common.hpp:307-406
+ *   sp24_compress        wgmma_sp_raw_common.hpp:140-205
+ *                        (compress_structured_sparse_a)
+ *   sp24_repack_meta     the per-tile metadata placement of
+ *                        wgmma_sp_raw_common.hpp:415-445 (smem_e_index*,
+ *                        e_thread_byte_offset*) re-targeted to tcgen05 TMEM
+ *   sp24_prune_2of4      (no counterpart: the reference only generates
+ *                        already-pruned A, wgmma_sp_raw_common.hpp:63-98)
+ */
+#ifndef SP24_H_
+#define SP24_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* sp24_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+typedef enum sp24_status {
+  SP24_OK = 0,
+  SP24_ERR_SHAPE = 1,      /* M/N/K or leading dimensions invalid (reference: run_case returns
+                              false, wgmma_sp_raw_common.hpp:1042-1045) */
+  SP24_ERR_ALIGN = 2,      /* pointer or stride breaks a 16-byte TMA rule and no workspace given */
+  SP24_ERR_NOT_2OF4 = 3,   /* a group of four does not hold exactly two nonzeros (reference exits,
+                              wgmma_sp_raw_common.hpp:163-166) */
+  SP24_ERR_ARCH = 4,       /* device is not sm_100 (reference gate: major < 9,
+                              wgmma_sp_raw_common.hpp:1115-1118) */
+  SP24_ERR_CUDA = 5,       /* a CUDA runtime call failed (reference: CHECK_CUDA exit, :17-25) */
+  SP24_ERR_TIMEOUT = 6,    /* a bounded device-side wait gave up; the kernel returned early */
+  SP24_ERR_NCCL = 7,       /* collective failure (multi-GPU all-gather) */
+  SP24_ERR_ARG = 8,        /* NULL pointer / bad enum */
+  SP24_ERR_WORKSPACE = 9   /* workspace missing or too small */
+} sp24_status;
+
+typedef enum sp24_dtype {
+  SP24_F16 = 0,   /* reference: half           (RawSparseConfig<half>, :300-309)          */
+  SP24_BF16 = 1,  /* reference: __nv_bfloat16  (RawSparseConfig<__nv_bfloat16>, :311-320) */
+  SP24_E4M3 = 2   /* reference: __nv_fp8_e4m3  (RawSparseConfig<__nv_fp8_e4m3>, :322-331) */
+} sp24_dtype;
+
+typedef enum sp24_meta_format {
+  /* The reference layout: M rows x K/8 bytes, row-major; group g of row r is the
+     low (g even) or high (g odd) nibble of byte r*(K/8) + g/2
+     (wgmma_sp_raw_common.hpp:197-202).  Needs workspace (repacked on the fly). */
+  SP24_META_REF = 0,
+  /* The tcgen05 image written by sp24_repack_meta (sp24_meta_tc_bytes bytes). */
+  SP24_META_TC = 1
+} sp24_meta_format;
+
+/* Output selection bits for sp24_gemm_desc.c_f32 / c_bf16: either may be NULL,
+   not both. */
+typedef struct sp24_gemm_desc {
+  sp24_dtype dtype;
+  int m, n, k;                 /* dense problem size                                  */
+  const void* a_c;             /* compressed A, m x k/2 elements, row stride lda_c      */
+  int64_t lda_c;               /* elements; 0 = k/2                                     */
+  const uint8_t* meta;         /* metadata in meta_format                               */
+  sp24_meta_format meta_format;
+  const void* b;               /* dense B, k x n elements, row stride ldb               */
+  int64_t ldb;                 /* elements; 0 = n                                       */
+  float* c_f32;                /* optional fp32 output, m x n, row stride ldc           */
+  void* c_bf16;                /* optional bf16 output, m x n, row stride ldc           */
+  int64_t ldc;                 /* elements; 0 = n                                       */
+  float alpha;                 /* C = alpha * (A*B); e4m3: 1/(scale_a*scale_b). 0 = 1.0 */
+  int tile_n;                  /* 0 = auto; 8..256 selects the reference's BlockN
+                                  variant (8 runs on the 16-wide tile)                  */
+  void* workspace;             /* device scratch for META_REF repack / B padding        */
+  size_t workspace_bytes;
+  int* status_dev;             /* optional device int: kernel writes nonzero on a
+                                  bounded-wait timeout; NULL = library-owned word        */
+} sp24_gemm_desc;
+
+/* Library / device queries ------------------------------------------------ */
+const char* sp24_version(void);
+const char* sp24_status_string(sp24_status s);
+/* SP24_OK if `device` is an sm_100 part the kernels were built for. */
+sp24_status sp24_check_device(int device);
+/* Bytes of the tcgen05 metadata image for an m x k A (padded to 128 x 128 atoms). */
+size_t sp24_meta_tc_bytes(int m, int k);
+/* Workspace sp24_gemm needs for this descriptor (0 if none). */
+size_t sp24_gemm_workspace_bytes(const sp24_gemm_desc* d);
+
+/* Compression: dense 2:4 A (m x k, row stride lda elements) -> A_c (m x k/2,
+   row stride ldac) + reference-layout metadata (m x k/8 bytes).
+   bad_dev: device int64 written with the first invalid group as
+   row*(k/4)+group, or -1 when every group is valid.  The call synchronises
+   `stream` and returns SP24_ERR_NOT_2OF4 when a group is invalid
+   (bad_host, if not NULL, receives the same value).
+   Reference: compress_structured_sparse_a, wgmma_sp_raw_common.hpp:140-205. */
+sp24_status sp24_compress(sp24_dtype dtype, const void* a_dense, int m, int k, int64_t lda,
+                          void* a_c, int64_t ldac, uint8_t* meta_ref, long long* bad_dev,
+                          long long* bad_host, sp24_stream_t stream);
+
+/* Magnitude 2:4 pruning: keep the two largest |a| of every group of four
+   (ties keep the lower index), zero the rest; writes the pruned dense A.
+   No reference counterpart (see file header). */
+sp24_status sp24_prune_2of4(sp24_dtype dtype, const void* a, int m, int k, int64_t lda,
+                            void* a_pruned, int64_t ldp, sp24_stream_t stream);
+
+/* Repack reference-layout metadata into the tcgen05 image consumed by
+   sp24_gemm with SP24_META_TC.  Padding groups get the valid code 0x4. */
+sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, int k,
+                             uint8_t* meta_tc, sp24_stream_t stream);
+
+/* The GEMM.  Reference: wgmma_sp_raw_kernel<Element,BlockN>
+   (wgmma_sp_raw_common.hpp:955-1030), grid (N/BlockN, M/64) x 128 threads,
+   fp32 C.  Preconditions of the reference (M%64, N%BlockN, K%32 / K%64 for
+   e4m3; :1042-1045) are relaxed to: k % 32 == 0 (k % 64 for e4m3), m,n >= 1. */
+sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream);
+
+/* Reads and clears the library-owned device status word that kernels raise
+   when a bounded wait timed out (used when sp24_gemm_desc.status_dev is NULL).
+   Synchronises `stream`.  SP24_ERR_TIMEOUT if a timeout happened.
+   (No reference counterpart: the reference never bounds a wait.) */
+sp24_status sp24_last_kernel_status(sp24_stream_t stream);
+
+/* Self-test of the bounded-wait path (no reference counterpart): launches the
+   GEMM of `d` with a producer that issues no load, so the consumers' waits run
+   out after `timeout_ns`; the kernel frees its TMEM and returns.  Requires
+   d->status_dev.  Synchronises; returns SP24_ERR_TIMEOUT (expected) or
+   SP24_OK if no wait ran out. */
+sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long timeout_ns,
+                                  sp24_stream_t stream);
+
+/* FP8 helpers for the e4m3 path.
+   sp24_amax_f32: amax_dev[0] = max |x| over count floats (device).
+   sp24_quantize_e4m3: q[i] = e4m3_rn_satfinite(x[i] * scale[0]) with
+   scale[0] = 448 / amax (computed on device from amax_dev). */
+sp24_status sp24_amax_f32(const float* x, size_t count, float* amax_dev, sp24_stream_t stream);
+sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_dev,
+                               float* scale_dev, uint8_t* q, sp24_stream_t stream);
+
+/* Multi-GPU N-sharding helpers (no collective on the GEMM path).
+   Columns [n0, n1) of C belong to `rank` of `world`; boundaries are multiples
+   of `align` (the tile width) except the last. */
+void sp24_shard_columns(int n, int world, int rank, int align, int* n0, int* n1);
+/* Column-block -> row-major permute after an all-gather of per-rank C shards:
+   src holds world blocks [rank][m][n1-n0] packed back to back (the shard of
+   rank r starts at element offset m*n0(r)); dst is m x n row-major. */
+sp24_status sp24_unshard_columns_f32(const float* src, float* dst, int m, int n, int world,
+                                     int align, sp24_stream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* SP24_H_ */

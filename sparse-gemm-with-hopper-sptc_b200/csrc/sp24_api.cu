@@ -1,0 +1,536 @@
+// sp24_api.cu — the C ABI declared in include/sp24.h: argument validation,
+// workspace handling, TMA tensor-map construction and kernel dispatch.
+//
+// Host-side contract mirrored from the reference harness
+// (wgmma_sp_raw_common.hpp:1032-1095): the caller owns every device buffer;
+// shape problems are reported instead of launched (:1042-1045); CUDA
+// failures become SP24_ERR_CUDA instead of exit(EXIT_FAILURE) (:17-25).
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/sp24.h"
+#include "sp24_gemm_kernel.cuh"
+#include "sp24_prep.cuh"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per bounded wait
+
+// Library-owned per-device status word used when the caller passes none.
+__device__ int g_sp24_status_word;
+
+#define SP24_CUDA_TRY(expr)                  \
+  do {                                       \
+    cudaError_t e__ = (expr);                \
+    if (e__ != cudaSuccess) {                \
+      (void)cudaGetLastError();              \
+      return SP24_ERR_CUDA;                  \
+    }                                        \
+  } while (0)
+
+inline cudaStream_t as_stream(sp24_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int esize(sp24_dtype dt) { return dt == SP24_E4M3 ? 1 : 2; }
+inline bool dtype_ok(int dt) { return dt == SP24_F16 || dt == SP24_BF16 || dt == SP24_E4M3; }
+inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+sp24_status get_encode_fn() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    (void)cudaGetLastError();
+  });
+  return g_encode ? SP24_OK : SP24_ERR_CUDA;
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int* status_word = nullptr;
+  bool ok = false;
+};
+
+std::mutex g_dev_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+sp24_status device_info(DeviceInfo** out) {
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return SP24_ERR_ARG;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& di = g_dev[dev];
+  if (!di.ok) {
+    cudaDeviceProp prop{};
+    SP24_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10 || prop.minor != 0) return SP24_ERR_ARCH;
+    di.sm_count = prop.multiProcessorCount;
+    void* p = nullptr;
+    SP24_CUDA_TRY(cudaGetSymbolAddress(&p, g_sp24_status_word));
+    di.status_word = static_cast<int*>(p);
+    di.ok = true;
+  }
+  *out = &di;
+  return SP24_OK;
+}
+
+sp24_status encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                      uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                      CUtensorMapSwizzle sw) {
+  sp24_status st = get_encode_fn();
+  if (st != SP24_OK) return st;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SP24_OK : SP24_ERR_ALIGN;
+}
+
+CUtensorMapSwizzle swizzle_for_span(int span) {
+  switch (span) {
+    case 128: return CU_TENSOR_MAP_SWIZZLE_128B;
+    case 64: return CU_TENSOR_MAP_SWIZZLE_64B;
+    case 32: return CU_TENSOR_MAP_SWIZZLE_32B;
+    default: return CU_TENSOR_MAP_SWIZZLE_NONE;
+  }
+}
+
+// Everything a launch needs after validation / workspace staging.
+struct Prepared {
+  sp24_dtype dt;
+  int m, n, k;
+  const void* a_c;
+  int64_t lda_c;
+  const uint8_t* meta_tc;
+  const void* b;
+  int64_t ldb;
+  float* c_f32;
+  void* c_bf16;
+  int64_t ldc;
+  float alpha;
+  int* status;
+  unsigned long long timeout_ns;
+  int stall_producer;
+};
+
+template <int DT, int BN>
+sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
+  using C = sp24::GemmCfg<DT, BN>;
+  auto kern = sp24::sp24_gemm_kernel<DT, BN>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    SP24_CUDA_TRY(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const CUtensorMapDataType tdt =
+      C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUtensorMap ta, tb;
+  sp24_status st =
+      encode_2d(&ta, tdt, p.a_c, static_cast<uint64_t>(p.k / 2), static_cast<uint64_t>(p.m),
+                static_cast<uint64_t>(p.lda_c) * C::ESZ, C::A_COLS, sp24::kBlockM,
+                CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st != SP24_OK) return st;
+  st = encode_2d(&tb, tdt, p.b, static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.k),
+                 static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::BKD,
+                 swizzle_for_span(C::B_SPAN));
+  if (st != SP24_OK) return st;
+
+  sp24::GemmParams P{};
+  P.m = p.m;
+  P.n = p.n;
+  P.k = p.k;
+  P.m_blocks = (p.m + sp24::kBlockM - 1) / sp24::kBlockM;
+  P.n_tiles = (p.n + BN - 1) / BN;
+  P.k_stages = (p.k + C::BKD - 1) / C::BKD;
+  P.num_tiles = P.m_blocks * P.n_tiles;
+  P.group_m = 16;
+  P.meta_tc = p.meta_tc;
+  P.c_f32 = p.c_f32;
+  P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
+  P.ldc = p.ldc;
+  P.alpha = p.alpha;
+  P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
+  P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
+  P.status = p.status;
+  P.timeout_ns = p.timeout_ns;
+  P.stall_producer = p.stall_producer;
+  const int grid = std::min(P.num_tiles, di.sm_count);
+  kern<<<grid, sp24::kThreads, C::SMEM_BYTES, stream>>>(ta, tb, P);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t);
+
+template <int DT>
+LaunchFn pick_bn(int bn) {
+  switch (bn) {
+    case 16: return launch_gemm<DT, 16>;
+    case 32: return launch_gemm<DT, 32>;
+    case 64: return launch_gemm<DT, 64>;
+    case 128: return launch_gemm<DT, 128>;
+    default: return launch_gemm<DT, 256>;
+  }
+}
+
+int choose_bn(int m, int n, int hint, int sm_count) {
+  if (hint > 0) {
+    if (hint <= 16) return 16;
+    if (hint <= 32) return 32;
+    if (hint <= 64) return 64;
+    if (hint <= 128) return 128;
+    return 256;
+  }
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  const long long mb = (m + 127) / 128;
+  const long long tiles256 = mb * ((n + 255) / 256);
+  return tiles256 >= sm_count ? 256 : 128;
+}
+
+struct WsPlan {
+  size_t meta_off = 0, meta_bytes = 0;
+  size_t b_off = 0, b_bytes = 0;
+  int64_t b_pitch_elems = 0;
+  size_t total = 0;
+};
+
+bool b_needs_copy(const sp24_gemm_desc* d) {
+  const int es = esize(d->dtype);
+  const int64_t ldb = d->ldb ? d->ldb : d->n;
+  return !aligned16(d->b) || ((ldb * es) % 16) != 0;
+}
+
+WsPlan plan_workspace(const sp24_gemm_desc* d) {
+  WsPlan w;
+  size_t off = 0;
+  if (d->meta_format == SP24_META_REF) {
+    w.meta_off = off;
+    w.meta_bytes = sp24_meta_tc_bytes(d->m, d->k);
+    off = round_up(off + w.meta_bytes, 256);
+  }
+  if (b_needs_copy(d)) {
+    const int es = esize(d->dtype);
+    w.b_pitch_elems = static_cast<int64_t>(round_up(static_cast<size_t>(d->n) * es, 16) / es);
+    w.b_off = off;
+    w.b_bytes = static_cast<size_t>(w.b_pitch_elems) * es * d->k;
+    off = round_up(off + w.b_bytes, 256);
+  }
+  w.total = off;
+  return w;
+}
+
+sp24_status validate(const sp24_gemm_desc* d) {
+  if (d == nullptr) return SP24_ERR_ARG;
+  if (!dtype_ok(d->dtype)) return SP24_ERR_ARG;
+  if (d->meta_format != SP24_META_REF && d->meta_format != SP24_META_TC) return SP24_ERR_ARG;
+  if (d->m <= 0 || d->n <= 0 || d->k <= 0) return SP24_ERR_SHAPE;
+  const int kq = d->dtype == SP24_E4M3 ? 64 : 32;
+  if (d->k % kq != 0) return SP24_ERR_SHAPE;
+  if (d->a_c == nullptr || d->meta == nullptr || d->b == nullptr) return SP24_ERR_ARG;
+  if (d->c_f32 == nullptr && d->c_bf16 == nullptr) return SP24_ERR_ARG;
+  const int64_t lda_c = d->lda_c ? d->lda_c : d->k / 2;
+  const int64_t ldb = d->ldb ? d->ldb : d->n;
+  const int64_t ldc = d->ldc ? d->ldc : d->n;
+  if (lda_c < d->k / 2 || ldb < d->n || ldc < d->n) return SP24_ERR_SHAPE;
+  if (!aligned16(d->a_c) || ((lda_c * esize(d->dtype)) % 16) != 0) return SP24_ERR_ALIGN;
+  if (!aligned16(d->meta)) return SP24_ERR_ALIGN;
+  if (d->tile_n < 0 || d->tile_n > 256) return SP24_ERR_ARG;
+  return SP24_OK;
+}
+
+sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned long long timeout_ns,
+                      int stall) {
+  sp24_status st = validate(d);
+  if (st != SP24_OK) return st;
+  DeviceInfo* di = nullptr;
+  st = device_info(&di);
+  if (st != SP24_OK) return st;
+  const WsPlan w = plan_workspace(d);
+  if (w.total > 0 && (d->workspace == nullptr || d->workspace_bytes < w.total))
+    return SP24_ERR_WORKSPACE;
+  if (w.total > 0 && !aligned16(d->workspace)) return SP24_ERR_ALIGN;
+  uint8_t* ws = static_cast<uint8_t*>(d->workspace);
+
+  Prepared p{};
+  p.dt = d->dtype;
+  p.m = d->m;
+  p.n = d->n;
+  p.k = d->k;
+  p.a_c = d->a_c;
+  p.lda_c = d->lda_c ? d->lda_c : d->k / 2;
+  p.b = d->b;
+  p.ldb = d->ldb ? d->ldb : d->n;
+  p.c_f32 = d->c_f32;
+  p.c_bf16 = d->c_bf16;
+  p.ldc = d->ldc ? d->ldc : d->n;
+  p.alpha = d->alpha == 0.0f ? 1.0f : d->alpha;
+  p.status = d->status_dev ? d->status_dev : di->status_word;
+  p.timeout_ns = timeout_ns;
+  p.stall_producer = stall;
+
+  if (d->meta_format == SP24_META_REF) {
+    st = sp24_repack_meta(d->dtype, d->meta, d->m, d->k, ws + w.meta_off,
+                          reinterpret_cast<sp24_stream_t>(stream));
+    if (st != SP24_OK) return st;
+    p.meta_tc = ws + w.meta_off;
+  } else {
+    p.meta_tc = d->meta;
+  }
+  if (w.b_bytes > 0) {
+    const int es = esize(d->dtype);
+    uint8_t* bp = ws + w.b_off;
+    SP24_CUDA_TRY(cudaMemsetAsync(bp, 0, w.b_bytes, stream));
+    SP24_CUDA_TRY(cudaMemcpy2DAsync(bp, static_cast<size_t>(w.b_pitch_elems) * es, d->b,
+                                    static_cast<size_t>(p.ldb) * es, static_cast<size_t>(d->n) * es,
+                                    static_cast<size_t>(d->k), cudaMemcpyDeviceToDevice, stream));
+    p.b = bp;
+    p.ldb = w.b_pitch_elems;
+  }
+
+  const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);
+  LaunchFn fn = d->dtype == SP24_F16    ? pick_bn<0>(bn)
+                : d->dtype == SP24_BF16 ? pick_bn<1>(bn)
+                                        : pick_bn<2>(bn);
+  return fn(p, *di, stream);
+}
+
+unsigned int grid_for(long long work, int block) {
+  long long g = (work + block - 1) / block;
+  if (g < 1) g = 1;
+  return static_cast<unsigned int>(std::min<long long>(g, 0x7FFFFFFF));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sp24_version(void) { return "sp24 0.1.0 (sm_100a tcgen05.mma.sp)"; }
+
+const char* sp24_status_string(sp24_status s) {
+  switch (s) {
+    case SP24_OK: return "ok";
+    case SP24_ERR_SHAPE: return "invalid shape";
+    case SP24_ERR_ALIGN: return "pointer or stride misaligned for TMA";
+    case SP24_ERR_NOT_2OF4: return "A is not 2:4 sparse";
+    case SP24_ERR_ARCH: return "device is not sm_100";
+    case SP24_ERR_CUDA: return "CUDA runtime error";
+    case SP24_ERR_TIMEOUT: return "bounded device wait timed out";
+    case SP24_ERR_NCCL: return "NCCL error";
+    case SP24_ERR_ARG: return "invalid argument";
+    case SP24_ERR_WORKSPACE: return "workspace missing or too small";
+  }
+  return "unknown status";
+}
+
+sp24_status sp24_check_device(int device) {
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SP24_ERR_CUDA;
+  }
+  return (prop.major == 10 && prop.minor == 0) ? SP24_OK : SP24_ERR_ARCH;
+}
+
+size_t sp24_meta_tc_bytes(int m, int k) {
+  if (m <= 0 || k <= 0) return 0;
+  const size_t mb = (static_cast<size_t>(m) + 127) / 128;
+  const size_t ka = (static_cast<size_t>(k) + 127) / 128;
+  return mb * ka * sp24::kAtomBytes;
+}
+
+size_t sp24_gemm_workspace_bytes(const sp24_gemm_desc* d) {
+  if (validate(d) != SP24_OK) return 0;
+  return plan_workspace(d).total;
+}
+
+sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream) {
+  return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0);
+}
+
+// Self-test of the bounded-wait path: runs the GEMM with a producer that
+// never issues a load, so the MMA and epilogue waits run out after
+// `timeout_ns`; the kernel returns and raises the status word.  Synchronises
+// `stream` and returns SP24_ERR_TIMEOUT when that happened (the expected
+// result), SP24_OK if it did not.
+sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long timeout_ns,
+                                  sp24_stream_t stream) {
+  if (d == nullptr || d->status_dev == nullptr) return SP24_ERR_ARG;
+  cudaStream_t s = as_stream(stream);
+  SP24_CUDA_TRY(cudaMemsetAsync(d->status_dev, 0, sizeof(int), s));
+  sp24_status st = gemm_impl(d, s, timeout_ns, 1);
+  if (st != SP24_OK) return st;
+  int h = 0;
+  SP24_CUDA_TRY(cudaMemcpyAsync(&h, d->status_dev, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SP24_CUDA_TRY(cudaStreamSynchronize(s));
+  return h ? SP24_ERR_TIMEOUT : SP24_OK;
+}
+
+sp24_status sp24_last_kernel_status(sp24_stream_t stream) {
+  DeviceInfo* di = nullptr;
+  sp24_status st = device_info(&di);
+  if (st != SP24_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  int h = 0;
+  SP24_CUDA_TRY(cudaMemcpyAsync(&h, di->status_word, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SP24_CUDA_TRY(cudaStreamSynchronize(s));
+  if (h) {
+    SP24_CUDA_TRY(cudaMemsetAsync(di->status_word, 0, sizeof(int), s));
+    SP24_CUDA_TRY(cudaStreamSynchronize(s));
+    return SP24_ERR_TIMEOUT;
+  }
+  return SP24_OK;
+}
+
+sp24_status sp24_compress(sp24_dtype dtype, const void* a_dense, int m, int k, int64_t lda,
+                          void* a_c, int64_t ldac, uint8_t* meta_ref, long long* bad_dev,
+                          long long* bad_host, sp24_stream_t stream) {
+  if (!dtype_ok(dtype) || a_dense == nullptr || a_c == nullptr || meta_ref == nullptr ||
+      bad_dev == nullptr)
+    return SP24_ERR_ARG;
+  if (m <= 0 || k <= 0 || k % 8 != 0) return SP24_ERR_SHAPE;
+  if (lda == 0) lda = k;
+  if (ldac == 0) ldac = k / 2;
+  if (lda < k || ldac < k / 2) return SP24_ERR_SHAPE;
+  const int es = esize(dtype);
+  const int need = es == 2 ? 16 : 8;
+  if ((reinterpret_cast<uintptr_t>(a_dense) % need) != 0 || (lda * es) % need != 0 ||
+      (reinterpret_cast<uintptr_t>(a_c) % (need / 2)) != 0 || (ldac * es) % (need / 2) != 0)
+    return SP24_ERR_ALIGN;
+  cudaStream_t s = as_stream(stream);
+  SP24_CUDA_TRY(cudaMemsetAsync(bad_dev, 0xFF, sizeof(long long), s));
+  const long long work = static_cast<long long>(m) * (k / 8);
+  const unsigned int g = grid_for(work, 256);
+  auto* bad = reinterpret_cast<unsigned long long*>(bad_dev);
+  const auto* a8 = static_cast<const uint8_t*>(a_dense);
+  auto* c8 = static_cast<uint8_t*>(a_c);
+  if (es == 2)
+    sp24::compress_kernel<2><<<g, 256, 0, s>>>(a8, m, k, lda * 2, c8, ldac * 2, meta_ref, bad);
+  else
+    sp24::compress_kernel<1><<<g, 256, 0, s>>>(a8, m, k, lda, c8, ldac, meta_ref, bad);
+  SP24_CUDA_TRY(cudaGetLastError());
+  long long h = -1;
+  SP24_CUDA_TRY(cudaMemcpyAsync(&h, bad_dev, sizeof(long long), cudaMemcpyDeviceToHost, s));
+  SP24_CUDA_TRY(cudaStreamSynchronize(s));
+  if (bad_host) *bad_host = h;
+  return h < 0 ? SP24_OK : SP24_ERR_NOT_2OF4;
+}
+
+sp24_status sp24_prune_2of4(sp24_dtype dtype, const void* a, int m, int k, int64_t lda,
+                            void* a_pruned, int64_t ldp, sp24_stream_t stream) {
+  if (!dtype_ok(dtype) || a == nullptr || a_pruned == nullptr) return SP24_ERR_ARG;
+  if (m <= 0 || k <= 0 || k % 4 != 0) return SP24_ERR_SHAPE;
+  if (lda == 0) lda = k;
+  if (ldp == 0) ldp = k;
+  if (lda < k || ldp < k) return SP24_ERR_SHAPE;
+  const int es = esize(dtype);
+  const int need = 4 * es;
+  if ((reinterpret_cast<uintptr_t>(a) % need) || (reinterpret_cast<uintptr_t>(a_pruned) % need) ||
+      (lda * es) % need || (ldp * es) % need)
+    return SP24_ERR_ALIGN;
+  cudaStream_t s = as_stream(stream);
+  const long long work = static_cast<long long>(m) * (k / 4);
+  const unsigned int g = grid_for(work, 256);
+  const auto* a8 = static_cast<const uint8_t*>(a);
+  auto* p8 = static_cast<uint8_t*>(a_pruned);
+  if (dtype == SP24_F16)
+    sp24::prune_kernel<0><<<g, 256, 0, s>>>(a8, m, k, lda * 2, p8, ldp * 2);
+  else if (dtype == SP24_BF16)
+    sp24::prune_kernel<1><<<g, 256, 0, s>>>(a8, m, k, lda * 2, p8, ldp * 2);
+  else
+    sp24::prune_kernel<2><<<g, 256, 0, s>>>(a8, m, k, lda, p8, ldp);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, int k,
+                             uint8_t* meta_tc, sp24_stream_t stream) {
+  if (!dtype_ok(dtype) || meta_ref == nullptr || meta_tc == nullptr) return SP24_ERR_ARG;
+  if (m <= 0 || k <= 0 || k % (dtype == SP24_E4M3 ? 64 : 32) != 0) return SP24_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(meta_tc) & 3u) != 0) return SP24_ERR_ALIGN;
+  const int mb = (m + 127) / 128;
+  const int ka = (k + 127) / 128;
+  const long long total = static_cast<long long>(ka) * mb * 128 * 4;
+  cudaStream_t s = as_stream(stream);
+  sp24::repack_meta_kernel<<<grid_for(total, 256), 256, 0, s>>>(
+      meta_ref, m, k, dtype == SP24_E4M3 ? 1 : 0, reinterpret_cast<uint32_t*>(meta_tc), mb, ka);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+sp24_status sp24_amax_f32(const float* x, size_t count, float* amax_dev, sp24_stream_t stream) {
+  if (x == nullptr || amax_dev == nullptr) return SP24_ERR_ARG;
+  cudaStream_t s = as_stream(stream);
+  SP24_CUDA_TRY(cudaMemsetAsync(amax_dev, 0, sizeof(float), s));
+  if (count == 0) return SP24_OK;
+  DeviceInfo* di = nullptr;
+  sp24_status st = device_info(&di);
+  if (st != SP24_OK) return st;
+  const unsigned int g = std::min<unsigned int>(grid_for(static_cast<long long>(count), 256),
+                                                static_cast<unsigned int>(di->sm_count) * 8u);
+  sp24::amax_kernel<<<g, 256, 0, s>>>(x, count, amax_dev);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_dev,
+                               float* scale_dev, uint8_t* q, sp24_stream_t stream) {
+  if (x == nullptr || amax_dev == nullptr || q == nullptr) return SP24_ERR_ARG;
+  if (count == 0) return SP24_OK;
+  DeviceInfo* di = nullptr;
+  sp24_status st = device_info(&di);
+  if (st != SP24_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  const unsigned int g = std::min<unsigned int>(grid_for(static_cast<long long>(count), 256),
+                                                static_cast<unsigned int>(di->sm_count) * 16u);
+  sp24::quantize_e4m3_kernel<<<g, 256, 0, s>>>(x, count, amax_dev, scale_dev, q);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+void sp24_shard_columns(int n, int world, int rank, int align, int* n0, int* n1) {
+  if (world < 1) world = 1;
+  if (align < 1) align = 1;
+  const int per_raw = (n + world - 1) / world;
+  const int per = (per_raw + align - 1) / align * align;
+  int a = std::min(rank * per, n);
+  int b = (rank == world - 1) ? n : std::min(a + per, n);
+  if (n0) *n0 = a;
+  if (n1) *n1 = b;
+}
+
+sp24_status sp24_unshard_columns_f32(const float* src, float* dst, int m, int n, int world,
+                                     int align, sp24_stream_t stream) {
+  if (src == nullptr || dst == nullptr || world < 1) return SP24_ERR_ARG;
+  if (m <= 0 || n <= 0) return SP24_ERR_SHAPE;
+  int n0 = 0, n1 = 0;
+  sp24_shard_columns(n, world, 0, align, &n0, &n1);
+  const int per = std::max(1, n1 - n0);
+  cudaStream_t s = as_stream(stream);
+  const long long total = static_cast<long long>(m) * n;
+  sp24::unshard_columns_kernel<<<grid_for(total, 256), 256, 0, s>>>(src, dst, m, n, world, per);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+}  // extern "C"

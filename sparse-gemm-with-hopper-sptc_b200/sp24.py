@@ -1,0 +1,246 @@
+"""ctypes binding of the sp24 C ABI (include/sp24.h) for tests and the bench.
+
+The product is the C-ABI shared library ``lib/libsp24.so`` built from
+``csrc/`` for sm_100a.  This module only marshals torch CUDA tensors into the
+plain pointers/sizes that ABI takes; every computation runs in the library's
+CUDA kernels.  There is no CPU path: if the library or a GPU is missing, the
+calls raise.
+
+Reference interfaces mirrored (codes1gn/sparse-gemm-with-hopper-sptc):
+  gemm()      wgmma_sp_raw_kernel<Element,BlockN>, wgmma_sp_raw_common.hpp:955-1030
+  compress()  compress_structured_sparse_a, wgmma_sp_raw_common.hpp:140-205
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import (POINTER, Structure, c_char_p, c_float, c_int, c_int64, c_longlong,
+                    c_size_t, c_uint8, c_ulonglong, c_void_p)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libsp24.so")
+
+F16, BF16, E4M3 = 0, 1, 2
+META_REF, META_TC = 0, 1
+
+STATUS = {
+    0: "SP24_OK", 1: "SP24_ERR_SHAPE", 2: "SP24_ERR_ALIGN", 3: "SP24_ERR_NOT_2OF4",
+    4: "SP24_ERR_ARCH", 5: "SP24_ERR_CUDA", 6: "SP24_ERR_TIMEOUT", 7: "SP24_ERR_NCCL",
+    8: "SP24_ERR_ARG", 9: "SP24_ERR_WORKSPACE",
+}
+
+# Every symbol include/sp24.h declares.
+EXPORTS = [
+    "sp24_version", "sp24_status_string", "sp24_check_device", "sp24_meta_tc_bytes",
+    "sp24_gemm_workspace_bytes", "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta",
+    "sp24_gemm", "sp24_last_kernel_status", "sp24_selftest_timeout", "sp24_amax_f32",
+    "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
+]
+
+
+class Sp24Error(RuntimeError):
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: {STATUS.get(code, code)}")
+
+
+class GemmDesc(Structure):
+    _fields_ = [
+        ("dtype", c_int), ("m", c_int), ("n", c_int), ("k", c_int),
+        ("a_c", c_void_p), ("lda_c", c_int64),
+        ("meta", c_void_p), ("meta_format", c_int),
+        ("b", c_void_p), ("ldb", c_int64),
+        ("c_f32", c_void_p), ("c_bf16", c_void_p), ("ldc", c_int64),
+        ("alpha", c_float), ("tile_n", c_int),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("status_dev", c_void_p),
+    ]
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the shared library (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} missing: run __graft_entry__.build() first")
+    lib = ctypes.CDLL(path)
+    lib.sp24_version.restype = c_char_p
+    lib.sp24_status_string.restype = c_char_p
+    lib.sp24_status_string.argtypes = [c_int]
+    lib.sp24_check_device.argtypes = [c_int]
+    lib.sp24_meta_tc_bytes.restype = c_size_t
+    lib.sp24_meta_tc_bytes.argtypes = [c_int, c_int]
+    lib.sp24_gemm_workspace_bytes.restype = c_size_t
+    lib.sp24_gemm_workspace_bytes.argtypes = [POINTER(GemmDesc)]
+    lib.sp24_gemm.argtypes = [POINTER(GemmDesc), c_void_p]
+    lib.sp24_selftest_timeout.argtypes = [POINTER(GemmDesc), c_ulonglong, c_void_p]
+    lib.sp24_last_kernel_status.argtypes = [c_void_p]
+    lib.sp24_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
+                                  c_void_p, c_void_p, POINTER(c_longlong), c_void_p]
+    lib.sp24_prune_2of4.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
+                                    c_void_p]
+    lib.sp24_repack_meta.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+    lib.sp24_amax_f32.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p]
+    lib.sp24_quantize_e4m3.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
+                                       c_void_p]
+    lib.sp24_shard_columns.restype = None
+    lib.sp24_shard_columns.argtypes = [c_int, c_int, c_int, c_int, POINTER(c_int),
+                                       POINTER(c_int)]
+    lib.sp24_unshard_columns_f32.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                             c_void_p]
+    for name in ("sp24_gemm", "sp24_selftest_timeout", "sp24_last_kernel_status",
+                 "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_amax_f32",
+                 "sp24_quantize_e4m3", "sp24_unshard_columns_f32", "sp24_check_device"):
+        getattr(lib, name).restype = c_int
+    _lib = lib
+    return lib
+
+
+def _check(code: int, where: str) -> None:
+    if code != 0:
+        raise Sp24Error(code, where)
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+def dtype_code(tdtype) -> int:
+    import torch
+    if tdtype == torch.float16:
+        return F16
+    if tdtype == torch.bfloat16:
+        return BF16
+    if tdtype in (torch.float8_e4m3fn, torch.uint8):
+        return E4M3
+    raise ValueError(f"unsupported dtype {tdtype}")
+
+
+def meta_tc_bytes(m: int, k: int) -> int:
+    return int(load().sp24_meta_tc_bytes(m, k))
+
+
+def compress(a_dense, stream=None):
+    """Dense 2:4 A (m x k, CUDA) -> (A_c m x k/2, reference metadata m x k/8 uint8)."""
+    import torch
+    lib = load()
+    m, k = a_dense.shape
+    a_c = torch.empty((m, k // 2), dtype=a_dense.dtype, device=a_dense.device)
+    meta = torch.empty((m, k // 8), dtype=torch.uint8, device=a_dense.device)
+    bad_dev = torch.empty(1, dtype=torch.int64, device=a_dense.device)
+    bad = c_longlong(-1)
+    code = lib.sp24_compress(dtype_code(a_dense.dtype), _ptr(a_dense), m, k, a_dense.stride(0),
+                             _ptr(a_c), a_c.stride(0), _ptr(meta), _ptr(bad_dev),
+                             ctypes.byref(bad), _stream(stream))
+    if code == 3:
+        err = Sp24Error(code, f"sp24_compress (first bad group {bad.value})")
+        err.bad_group = bad.value
+        raise err
+    _check(code, "sp24_compress")
+    return a_c, meta
+
+
+def prune_2of4(a, stream=None):
+    import torch
+    lib = load()
+    m, k = a.shape
+    out = torch.empty_like(a)
+    _check(lib.sp24_prune_2of4(dtype_code(a.dtype), _ptr(a), m, k, a.stride(0), _ptr(out),
+                               out.stride(0), _stream(stream)), "sp24_prune_2of4")
+    return out
+
+
+def repack_meta(meta_ref, m: int, k: int, dtype, stream=None):
+    import torch
+    lib = load()
+    out = torch.empty(meta_tc_bytes(m, k), dtype=torch.uint8, device=meta_ref.device)
+    _check(lib.sp24_repack_meta(dtype_code(dtype), _ptr(meta_ref), m, k, _ptr(out),
+                                _stream(stream)), "sp24_repack_meta")
+    return out
+
+
+def make_desc(a_c, meta, b, m, n, k, *, meta_format=META_REF, c_f32=None, c_bf16=None,
+              alpha=1.0, tile_n=0, workspace=None, status=None, dtype=None) -> GemmDesc:
+    d = GemmDesc()
+    d.dtype = dtype_code(dtype if dtype is not None else a_c.dtype)
+    d.m, d.n, d.k = m, n, k
+    d.a_c, d.lda_c = _ptr(a_c), a_c.stride(0)
+    d.meta, d.meta_format = _ptr(meta), meta_format
+    d.b, d.ldb = _ptr(b), b.stride(0)
+    d.c_f32, d.c_bf16 = _ptr(c_f32), _ptr(c_bf16)
+    ref = c_f32 if c_f32 is not None else c_bf16
+    d.ldc = ref.stride(0)
+    d.alpha = alpha
+    d.tile_n = tile_n
+    d.workspace = _ptr(workspace)
+    d.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    d.status_dev = _ptr(status)
+    return d
+
+
+def workspace_bytes(desc: GemmDesc) -> int:
+    return int(load().sp24_gemm_workspace_bytes(ctypes.byref(desc)))
+
+
+def gemm(a_c, meta, b, m, n, k, *, meta_format=META_REF, out_f32=True, out_bf16=False,
+         alpha=1.0, tile_n=0, workspace=None, c_f32=None, c_bf16=None, stream=None,
+         dtype=None):
+    """C = alpha * decompress(A_c, meta) @ B through sp24_gemm.  Returns (c_f32, c_bf16)."""
+    import torch
+    lib = load()
+    dev = a_c.device
+    if out_f32 and c_f32 is None:
+        c_f32 = torch.empty((m, n), dtype=torch.float32, device=dev)
+    if out_bf16 and c_bf16 is None:
+        c_bf16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    d = make_desc(a_c, meta, b, m, n, k, meta_format=meta_format, c_f32=c_f32, c_bf16=c_bf16,
+                  alpha=alpha, tile_n=tile_n, workspace=workspace, dtype=dtype)
+    need = workspace_bytes(d)
+    if need and (workspace is None or d.workspace_bytes < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        d.workspace, d.workspace_bytes = workspace.data_ptr(), need
+    _check(lib.sp24_gemm(ctypes.byref(d), _stream(stream)), "sp24_gemm")
+    return c_f32, c_bf16
+
+
+def last_kernel_status(stream=None) -> int:
+    return int(load().sp24_last_kernel_status(_stream(stream)))
+
+
+def amax_quantize_e4m3(x, stream=None):
+    """fp32 CUDA tensor -> (e4m3 bits as uint8, scale tensor[1]) with scale = 448/amax."""
+    import torch
+    lib = load()
+    amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    q = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    s = _stream(stream)
+    _check(lib.sp24_amax_f32(_ptr(x), x.numel(), _ptr(amax), s), "sp24_amax_f32")
+    _check(lib.sp24_quantize_e4m3(_ptr(x), x.numel(), _ptr(amax), _ptr(scale), _ptr(q), s),
+           "sp24_quantize_e4m3")
+    return q, scale
+
+
+def shard_columns(n: int, world: int, rank: int, align: int):
+    a, b = c_int(0), c_int(0)
+    load().sp24_shard_columns(n, world, rank, align, ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value
+
+
+def unshard_columns_f32(src, m: int, n: int, world: int, align: int, stream=None):
+    import torch
+    dst = torch.empty((m, n), dtype=torch.float32, device=src.device)
+    _check(load().sp24_unshard_columns_f32(_ptr(src), _ptr(dst), m, n, world, align,
+                                           _stream(stream)), "sp24_unshard_columns_f32")
+    return dst
