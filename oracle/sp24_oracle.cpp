@@ -249,13 +249,14 @@ void oracle_prune_2of4(int dt, const void* a, int m, int k, void* out) {
     }
 }
 
-// tcgen05 metadata image: [ceil(k/128)][ceil(m/128)][128 lanes][4 x u32].
+// tcgen05 metadata image: [ceil(k/128)][mb][128 lanes][4 x u32], mb = ceil(m/128)
+// rounded up to even (a CTA pair always finds an atom for its second half).
 //  16-bit types: lane L = 16*m2 + 8*k1 + m0, word w holds in bits [16h, 16h+16)
 //    the 16 dense-K run [128*ka + 32*w + 16*k1, +16) of row 16*m2 + 8*h + m0.
 //  e4m3: lane L = row L, 16 bytes = the row's reference bytes of the atom.
 // Padding (rows >= m or K >= k) holds the valid code 0x4 in every nibble.
 void oracle_meta_tc_image(int dt, const uint8_t* meta, int m, int k, uint32_t* img) {
-  const int mb_n = (m + 127) / 128, ka_n = (k + 127) / 128, rb = k / 8;
+  const int mb_n = ((m + 127) / 128 + 1) / 2 * 2, ka_n = (k + 127) / 128, rb = k / 8;
   for (int ka = 0; ka < ka_n; ++ka)
     for (int mb = 0; mb < mb_n; ++mb)
       for (int L = 0; L < 128; ++L)

@@ -10,10 +10,12 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/sp24.h"
+#include "sp24_gemm2sm_kernel.cuh"
 #include "sp24_gemm_kernel.cuh"
 #include "sp24_prep.cuh"
 
@@ -40,6 +42,11 @@ inline int esize(sp24_dtype dt) { return dt == SP24_E4M3 ? 1 : 2; }
 inline bool dtype_ok(int dt) { return dt == SP24_F16 || dt == SP24_BF16 || dt == SP24_E4M3; }
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
+// 128-row blocks of the tcgen05 metadata image, padded to an even count so a
+// CTA pair's second half always has an atom to load.
+inline int meta_mblocks(int m) { return ((m + 127) / 128 + 1) / 2 * 2; }
+inline int meta_katoms(int k) { return (k + 127) / 128; }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -163,6 +170,7 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.num_tiles = P.m_blocks * P.n_tiles;
   P.group_m = 16;
   P.meta_tc = p.meta_tc;
+  P.meta_mblocks = meta_mblocks(p.m);
   P.c_f32 = p.c_f32;
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
   P.ldc = p.ldc;
@@ -176,6 +184,79 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   kern<<<grid, sp24::kThreads, C::SMEM_BYTES, stream>>>(ta, tb, P);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
+}
+
+
+template <int DT>
+sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
+  using C = sp24::PairCfg<DT>;
+  auto kern = sp24::sp24_gemm2sm_kernel<DT>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    SP24_CUDA_TRY(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const CUtensorMapDataType tdt =
+      C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUtensorMap ta, tb, te;
+  sp24_status st =
+      encode_2d(&ta, tdt, p.a_c, static_cast<uint64_t>(p.k / 2), static_cast<uint64_t>(p.m),
+                static_cast<uint64_t>(p.lda_c) * C::ESZ, C::A_COLS, sp24::kBlockM,
+                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SP24_OK) return st;
+  st = encode_2d(&tb, tdt, p.b, static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.k),
+                 static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::BKD,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SP24_OK) return st;
+  const int mblk = meta_mblocks(p.m);
+  const uint64_t lanes = static_cast<uint64_t>(meta_katoms(p.k)) * mblk * 128;
+  st = encode_2d(&te, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.meta_tc, 16, lanes, 16, 16, 128,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != SP24_OK) return st;
+
+  sp24::PairParams P{};
+  P.m = p.m;
+  P.n = p.n;
+  P.k = p.k;
+  P.m_blocks = mblk;
+  P.m_pairs = (p.m + 255) / 256;
+  P.n_tiles = (p.n + 255) / 256;
+  P.k_stages = (p.k + C::BKD - 1) / C::BKD;
+  P.num_tiles = P.m_pairs * P.n_tiles;
+  P.group_m = 8;
+  P.c_f32 = p.c_f32;
+  P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
+  P.ldc = p.ldc;
+  P.alpha = p.alpha;
+  P.vec_f32 = p.c_f32 == nullptr                            ? 0
+              : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
+              : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
+                                                            : 0;
+  P.vec_bf16 = p.c_bf16 == nullptr                          ? 0
+               : (aligned32(p.c_bf16) && (p.ldc % 16) == 0) ? 2
+               : (aligned16(p.c_bf16) && (p.ldc % 8) == 0)  ? 1
+                                                            : 0;
+  P.status = p.status;
+  P.timeout_ns = p.timeout_ns;
+  P.stall_producer = p.stall_producer;
+  const int pairs = std::max(1, std::min(P.num_tiles, di.sm_count / 2));
+  kern<<<2 * pairs, sp24::kPairThreads, C::SMEM_BYTES, stream>>>(ta, tb, te, P);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+// Kernel choice: the CTA-pair kernel for problems with at least one full
+// 256 x 256 tile, the single-CTA kernel (narrow N tiles) otherwise.
+// SP24_KERNEL=1sm|2sm overrides (benchmarks and tests).
+bool use_pair_kernel(int m, int n, int hint) {
+  const char* env = std::getenv("SP24_KERNEL");
+  if (env != nullptr && std::strcmp(env, "1sm") == 0) return false;
+  if (env != nullptr && std::strcmp(env, "2sm") == 0) return true;
+  if (hint != 0 && hint != 256) return false;
+  return m >= 256 && n >= 256;
 }
 
 using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t);
@@ -308,6 +389,12 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     p.ldb = w.b_pitch_elems;
   }
 
+  if (use_pair_kernel(d->m, d->n, d->tile_n)) {
+    LaunchFn pf = d->dtype == SP24_F16    ? launch_gemm2sm<0>
+                  : d->dtype == SP24_BF16 ? launch_gemm2sm<1>
+                                          : launch_gemm2sm<2>;
+    return pf(p, *di, stream);
+  }
   const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);
   LaunchFn fn = d->dtype == SP24_F16    ? pick_bn<0>(bn)
                 : d->dtype == SP24_BF16 ? pick_bn<1>(bn)
@@ -354,9 +441,7 @@ sp24_status sp24_check_device(int device) {
 
 size_t sp24_meta_tc_bytes(int m, int k) {
   if (m <= 0 || k <= 0) return 0;
-  const size_t mb = (static_cast<size_t>(m) + 127) / 128;
-  const size_t ka = (static_cast<size_t>(k) + 127) / 128;
-  return mb * ka * sp24::kAtomBytes;
+  return static_cast<size_t>(meta_mblocks(m)) * meta_katoms(k) * sp24::kAtomBytes;
 }
 
 size_t sp24_gemm_workspace_bytes(const sp24_gemm_desc* d) {
@@ -468,8 +553,8 @@ sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, i
   if (!dtype_ok(dtype) || meta_ref == nullptr || meta_tc == nullptr) return SP24_ERR_ARG;
   if (m <= 0 || k <= 0 || k % (dtype == SP24_E4M3 ? 64 : 32) != 0) return SP24_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(meta_tc) & 3u) != 0) return SP24_ERR_ALIGN;
-  const int mb = (m + 127) / 128;
-  const int ka = (k + 127) / 128;
+  const int mb = meta_mblocks(m);
+  const int ka = meta_katoms(k);
   const long long total = static_cast<long long>(ka) * mb * 128 * 4;
   cudaStream_t s = as_stream(stream);
   sp24::repack_meta_kernel<<<grid_for(total, 256), 256, 0, s>>>(

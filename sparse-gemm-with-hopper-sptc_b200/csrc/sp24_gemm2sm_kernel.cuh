@@ -1,0 +1,383 @@
+// sp24_gemm2sm_kernel.cuh — the large-problem 2:4 sparse GEMM: a CTA pair
+// (cluster of 2) computes a 256 x 256 tile with tcgen05.mma.sp.cta_group::2.
+//
+// Why a pair: one tcgen05.mma.sp.cta_group::2 with M=256, N=256 reads A_c
+// rows 0-127 and B columns 0-127 from CTA 0's shared memory and A_c rows
+// 128-255 and B columns 128-255 from CTA 1's.  Each SM therefore stages half
+// of B, which (a) halves B's share of the L2->SM traffic and of the shared
+// memory read bandwidth per MMA and (b) lets the same shared-memory ring cover
+// twice the MMA time.  The single-CTA kernel (sp24_gemm_kernel.cuh) was
+// bound by bytes in flight per SM; this one carries 1.6x the FLOPs per staged
+// byte.  No TMA multicast is used: each CTA loads its own tiles.
+//
+// Roles per CTA (10 warps):
+//   warp 0      TMA producer (both CTAs): A_c rows / B half-columns / the
+//               metadata atom of its own 128 rows; completion bytes of both
+//               CTAs are counted on the leader's (rank 0) full barrier, which
+//               only the leader arms.
+//   warp 1      TMEM owner (alloc/dealloc with cta_group::2 in both CTAs);
+//               in the leader one lane issues tcgen05.cp (metadata of both
+//               CTAs into their own TMEM) and the pair MMAs, and commits with
+//               a 2-CTA multicast so both CTAs' ring slots / accumulator
+//               barriers advance.
+//   warps 2-9   epilogue (both CTAs): two warps per TMEM lane quarter, each
+//               pulls 128 accumulator columns of its 32 rows into registers,
+//               hands the accumulator back to the leader's MMA warp at once
+//               (remote mbarrier arrive), then scales / converts / stores
+//               while the next tile's MMAs run.
+// The accumulator (256 columns) plus two metadata buffers (8 columns) fill
+// TMEM, so the accumulator is single-buffered; the register hand-off keeps
+// the MMA pause to the TMEM read time.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "sp24_gemm_kernel.cuh"
+#include "sp24_ptx.cuh"
+
+namespace sp24 {
+
+constexpr int kPairThreads = 320;
+constexpr int kPairEpiWarps = 8;
+
+struct PairParams {
+  int m, n, k;
+  int m_blocks;   // 128-row blocks of the metadata image (padded to even)
+  int m_pairs;    // 256-row tiles
+  int n_tiles;    // 256-column tiles
+  int k_stages, num_tiles, group_m;
+  float* c_f32;
+  __nv_bfloat16* c_bf16;
+  long long ldc;
+  float alpha;
+  int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
+  int vec_bf16;
+  int* status;
+  unsigned long long timeout_ns;
+  int stall_producer;
+};
+
+template <int DT>
+struct PairCfg {
+  static constexpr int ESZ = (DT == 2) ? 1 : 2;
+  static constexpr int KIND = (DT == 2) ? 1 : 0;
+  static constexpr int BKD = (DT == 2) ? 256 : 128;     // dense K per stage
+  static constexpr int MMA_K = (DT == 2) ? 64 : 32;     // dense K per MMA
+  static constexpr int MMAS = BKD / MMA_K;              // 4 MMAs per stage
+  static constexpr int ATOMS = BKD / 128;               // metadata atoms per stage
+  static constexpr int A_COLS = 128 / ESZ;              // compressed values per stage row
+  static constexpr int A_BYTES = kBlockM * 128;         // SW128 K-major
+  static constexpr int BN = 256;                        // pair tile width
+  static constexpr int BN_CTA = 128;                    // B columns staged per CTA
+  static constexpr int B_BOXN = 128 / ESZ;
+  static constexpr int B_BOXES = BN_CTA / B_BOXN;
+  static constexpr int B_BOX_BYTES = 128 * BKD;
+  static constexpr int B_BYTES = B_BOX_BYTES * B_BOXES;
+  static constexpr uint32_t B_LBO = B_BOX_BYTES;        // MN-major SW128: chunk stride
+  static constexpr uint32_t B_SBO = 1024;               // 8-row K group stride
+  static constexpr int B_MMA_ADVANCE = MMA_K * 128;
+  static constexpr int E_BYTES = ATOMS * kAtomBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
+  static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int LOADS = 1 + B_BOXES + ATOMS;     // TMA boxes per stage per CTA
+  static constexpr int E_COL = 256;                     // two buffers of ATOMS*4 columns
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
+  static constexpr uint32_t IDESC = make_idesc_sparse(FMT, 256, 256, true);
+  static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
+  static_assert(STAGES >= 3, "pair kernel wants a deep ring");
+  static_assert(LOADS <= 32, "one lane per TMA box");
+};
+
+SP24_DEV void pair_tile_coords(const PairParams& P, int t, int& mp, int& nb) {
+  const int per_group = P.group_m * P.n_tiles;
+  const int g = t / per_group;
+  const int first = g * P.group_m;
+  const int gm = min(P.m_pairs - first, P.group_m);
+  const int r = t - g * per_group;
+  mp = first + r % gm;
+  nb = r / gm;
+}
+
+SP24_DEV void st_global_v8_u32(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+// Store 128 consecutive accumulator columns of one row (already in registers).
+SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, int col0) {
+  if (row >= P.m) return;
+  const float alpha = P.alpha;
+  const bool full = col0 + 128 <= P.n;
+  if (P.c_f32 != nullptr) {
+    float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col0;
+    if (full && P.vec_f32 == 2) {
+#pragma unroll
+      for (int i = 0; i < 128; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]) * alpha;
+        st_global_v8(dst + i, v);
+      }
+    } else if (full && P.vec_f32 == 1) {
+#pragma unroll
+      for (int i = 0; i < 128; i += 4)
+        *reinterpret_cast<float4*>(dst + i) =
+            make_float4(__uint_as_float(r[i]) * alpha, __uint_as_float(r[i + 1]) * alpha,
+                        __uint_as_float(r[i + 2]) * alpha, __uint_as_float(r[i + 3]) * alpha);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]) * alpha;
+    }
+  }
+  if (P.c_bf16 != nullptr) {
+    __nv_bfloat16* dst = P.c_bf16 + static_cast<long long>(row) * P.ldc + col0;
+    if (full && P.vec_bf16 >= 1) {
+#pragma unroll
+      for (int i = 0; i < 128; i += 16) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[i + 2 * j]) * alpha,
+                                                   __uint_as_float(r[i + 2 * j + 1]) * alpha);
+          pk[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        if (P.vec_bf16 == 2) {
+          st_global_v8_u32(dst + i, pk);
+        } else {
+          *reinterpret_cast<uint4*>(dst + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(dst + i + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (col0 + i < P.n) dst[i] = __float2bfloat16_rn(__uint_as_float(r[i]) * alpha);
+    }
+  }
+}
+
+template <int DT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    sp24_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmE, const PairParams P) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using C = PairCfg<DT>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t accf_bar;
+  __shared__ __align__(8) uint64_t acce_bar;
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&accf_bar, 1);
+    mbar_init(&acce_bar, 2 * kPairEpiWarps);
+    mbar_init(&drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmE);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  const uint64_t tmo = P.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // The whole warp runs the loop; lane i issues the i-th TMA box of a stage
+    // (A_c, B chunks, metadata atoms), so one warp instruction covers a stage.
+    if (!P.stall_producer) {
+      const uint32_t full0_leader = mapa_shared(smem_u32(&full_bar[0]), 0);
+      const CUtensorMap* lane_map =
+          lane == 0 ? &tmA : (lane <= C::B_BOXES ? &tmB : &tmE);
+      const int lb = lane - 1;                    // B chunk of lanes 1..B_BOXES
+      const int la = lane - 1 - C::B_BOXES;       // metadata atom of the last lanes
+      const uint32_t lane_off =
+          lane == 0 ? 0u
+                    : (lane <= C::B_BOXES ? static_cast<uint32_t>(C::A_BYTES + lb * C::B_BOX_BYTES)
+                                          : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES +
+                                                                  la * kAtomBytes));
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      uint32_t armed_mask = 0, armed_ph = 0;
+      for (int t = pair; t < P.num_tiles && ok; t += npairs) {
+        int mp, nb;
+        pair_tile_coords(P, t, mp, nb);
+        const int row0 = mp * 256 + static_cast<int>(rank) * 128;
+        const int col0 = nb * 256 + static_cast<int>(rank) * 128 + lb * C::B_BOXN;
+        const int mb = mp * 2 + static_cast<int>(rank);
+        for (int ks = 0; ks < P.k_stages; ++ks) {
+          int good = 1;
+          if (lane == 0) good = mbar_wait_fast(&empty_bar[s], ph ^ 1u, &abort_sh, tmo) ? 1 : 0;
+          if (__shfl_sync(0xffffffffu, good, 0) == 0) {
+            ok = false;
+            break;
+          }
+          if (leader && lane == 0) {
+            mbar_arrive_expect_tx(&full_bar[s], 2u * C::STAGE_BYTES);
+            armed_mask |= 1u << s;
+            armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
+          }
+          __syncwarp();
+          if (lane < C::LOADS) {
+            int x, y;
+            if (lane == 0) {
+              x = ks * C::A_COLS;
+              y = row0;
+            } else if (lane <= C::B_BOXES) {
+              x = col0;
+              y = ks * C::BKD;
+            } else {
+              x = 0;
+              y = ((ks * C::ATOMS + la) * P.m_blocks + mb) * 128;
+            }
+            tma_load_2d_pair(smem + s * C::STAGE_BYTES + lane_off, lane_map,
+                             full0_leader + static_cast<uint32_t>(s * sizeof(uint64_t)), x, y);
+          }
+          if (++s == C::STAGES) s = 0, ph ^= 1u;
+        }
+      }
+      if (!ok && leader && lane == 0) {
+        volatile int dummy = 0;
+        for (int i = 0; i < C::STAGES; ++i)
+          if (armed_mask & (1u << i)) mbar_wait(&full_bar[i], (armed_ph >> i) & 1u, &dummy, tmo);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    // Descriptors are formed once; per stage only the start-address field
+    // moves (stage offset >> 4 added to the 64-bit descriptor), per MMA by a
+    // compile-time step.  Metadata: atom a of a stage lives in TMEM columns
+    // E_COL + ebuf*ATOMS*4 + a*4; kind::f16 MMAs use one column each (odd
+    // columns through the sparsity selector), kind::f8f6f4 MMAs two.
+    if (leader && lane == 0) {
+      const uint32_t smem_base = smem_u32(smem);
+      const uint64_t adesc0 = make_sdesc(smem_base, 16, 1024, kLayoutSW128);
+      const uint64_t bdesc0 = make_sdesc(smem_base + C::A_BYTES, C::B_LBO, C::B_SBO, kLayoutSW128);
+      const uint64_t edesc0 =
+          make_sdesc(smem_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
+      constexpr uint32_t SD = C::STAGE_BYTES >> 4;
+      int s = 0;
+      uint32_t ph = 0, soff = 0, aph = 0, ebuf = 0;
+      bool ok = true, any = false;
+      for (int t = pair; t < P.num_tiles && ok; t += npairs) {
+        if (!mbar_wait_fast<true>(&acce_bar, aph ^ 1u, &abort_sh, tmo)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int ks = 0; ks < P.k_stages; ++ks) {
+          if (!mbar_wait_fast(&full_bar[s], ph, &abort_sh, tmo)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
+#pragma unroll
+          for (int a = 0; a < C::ATOMS; ++a)
+            tc_cp_128x128b_pair(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
+          const int kleft = P.k - ks * C::BKD;
+          const uint32_t acc0 = ks > 0 ? 1u : 0u;
+#pragma unroll
+          for (int j = 0; j < C::MMAS; ++j) {
+            if (j * C::MMA_K < kleft) {
+              constexpr int kPerAtom = 128 / C::MMA_K;
+              const int a = j / kPerAtom;
+              const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(j % kPerAtom)
+                                                  : static_cast<uint32_t>(2 * (j % kPerAtom));
+              const uint32_t eaddr = e_tmem + 4u * a + (col & ~1u);
+              tc_mma_sp_pair<C::KIND>(tmem_base, adesc0 + soff + j * 2,
+                                      bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4), eaddr,
+                                      C::IDESC | (col & 1u), j > 0 ? 1u : acc0);
+            }
+          }
+          any = true;
+          tc_commit_pair(&empty_bar[s], static_cast<uint16_t>(3));
+          ebuf ^= static_cast<uint32_t>(C::ATOMS * 4);
+          soff += SD;
+          if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
+        }
+        if (!ok) break;
+        tc_commit_pair(&accf_bar, static_cast<uint16_t>(3));
+        aph ^= 1u;
+      }
+      if (!ok && any) {
+        volatile int dummy = 0;
+        tc_commit_pair(&drain_bar, static_cast<uint16_t>(1));
+        mbar_wait(&drain_bar, 0, &dummy, tmo);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t acce_leader = mapa_shared(smem_u32(&acce_bar), 0);
+    uint32_t aph = 0;
+    for (int t = pair; t < P.num_tiles; t += npairs) {
+      int mp, nb;
+      pair_tile_coords(P, t, mp, nb);
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&accf_bar, aph, &abort_sh, tmo);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                          static_cast<uint32_t>(half * 128);
+      uint32_t r[128];
+      tmem_ld_x32(tb + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_x32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld_x32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld_x32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_ld_wait(r);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_leader);
+      const int row = mp * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      pair_store_row(P, r, row, nb * 256 + half * 128);
+      aph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && abort_sh != 0 && P.status != nullptr) atomicExch(P.status, 1);
+#endif
+}
+
+}  // namespace sp24

@@ -45,7 +45,8 @@ struct GemmParams {
   int m, n, k;
   int m_blocks, n_tiles, k_stages, num_tiles;
   int group_m;
-  const uint8_t* meta_tc;  // tcgen05 metadata image [k_atoms][m_blocks][128][16 B]
+  const uint8_t* meta_tc;  // tcgen05 metadata image [k_atoms][meta_mblocks][128][16 B]
+  int meta_mblocks;        // 128-row blocks in the image (m_blocks rounded up to even)
   float* c_f32;
   __nv_bfloat16* c_bf16;
   long long ldc;
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (with_e) {
             const int ka = ks / C::STAGES_PER_ATOM;
             const uint8_t* src =
-                P.meta_tc + (static_cast<size_t>(ka) * P.m_blocks + mb) * kAtomBytes;
+                P.meta_tc + (static_cast<size_t>(ka) * P.meta_mblocks + mb) * kAtomBytes;
             bulk_load(st + C::A_BYTES + C::B_BYTES, src, kAtomBytes, &full_bar[s]);
           }
           if (++s == C::STAGES) s = 0, ph ^= 1u;

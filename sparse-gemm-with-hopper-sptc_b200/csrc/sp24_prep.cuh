@@ -139,7 +139,8 @@ __global__ void prune_kernel(const uint8_t* __restrict__ a, int m, int k, long l
 
 // Reference metadata (row-major, k/8 bytes per row) -> tcgen05 image.
 // Image: [k_atoms][m_blocks][128 lanes][4 x u32]; one atom covers 128 rows x
-// 128 dense K.  Word w of lane L is TMEM column w of the atom.
+// 128 dense K; m_blocks = ceil(m/128) rounded up to even so that a CTA pair's
+// second 128 rows always have an atom.  Word w of lane L is TMEM column w.
 //  16-bit types (kind::f16, one column per K=32 MMA):
 //    L = 16*m2 + 8*k1 + m0;  bits [0,16)  = row 16*m2 + m0,     K [32w+16k1, +16)
 //                            bits [16,32) = row 16*m2 + 8 + m0, same K range

@@ -3,10 +3,10 @@
 // (TMEM allocation, tcgen05.cp, tcgen05.mma.sp, tcgen05.commit, tcgen05.ld).
 //
 // Everything here is written from the PTX ISA description of the instructions.
-// Every spin-wait is bounded: a wait gives up after kWaitTimeoutNs of
-// %globaltimer (or kWaitMaxIters polls), raises a CTA-wide abort flag and
-// returns false, so a broken pipeline turns into an error status instead of a
-// hung GPU.
+// Every spin-wait is bounded: a wait gives up after the caller's timeout of
+// %globaltimer (or 2^26 polls), raises a CTA-wide abort flag and returns
+// false, so a broken pipeline turns into an error status instead of a hung
+// GPU.
 #pragma once
 
 #include <cuda.h>
@@ -50,27 +50,67 @@ SP24_DEV void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
+// kCluster: acquire at cluster scope (the phase was completed by arrivals
+// from another CTA of the cluster that released at cluster scope).
+template <bool kCluster = false>
 SP24_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
+  if constexpr (kCluster) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 
-// Bounded wait for the phase of parity `parity` to complete.  Returns false
-// (and raises *abort) when the wait times out, or when another role of the
-// CTA already raised *abort.
-SP24_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait, kept out of line so the issue loops stay short.
+template <bool kCluster>
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                            uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t it = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kCluster>(bar, parity)) return true;
+    if ((++it & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > timeout_ns || it > (1u << 26)) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for the phase of parity `parity` to complete: one inline
+// try_wait (itself a bounded hardware wait), then the out-of-line loop.
+// Returns false (and raises *abort) when the wait times out, or when another
+// role of the CTA already raised *abort.
+template <bool kCluster = false>
+SP24_DEV bool mbar_wait_fast(uint64_t* bar, uint32_t parity, volatile int* abort,
+                             uint64_t timeout_ns) {
+  if (__builtin_expect(mbar_try_wait<kCluster>(bar, parity), 1)) return true;
+  return mbar_wait_slow<kCluster>(bar, parity, abort, timeout_ns);
+}
+
+template <bool kCluster = false>
+SP24_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t timeout_ns) {
+  if (mbar_try_wait<kCluster>(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait<kCluster>(bar, parity)) return true;
     if ((++it & 63u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > timeout_ns || it > (1u << 26)) {
@@ -185,6 +225,88 @@ SP24_DEV void tmem_ld_wait(uint32_t (&r)[N]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// ---------------------------------------------------------------- clusters / CTA pairs
+SP24_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared variable in CTA `rank` of the cluster.
+SP24_DEV uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+SP24_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+SP24_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// TMA load issued by either CTA of a pair; completion bytes go to the
+// mbarrier at `bar_cluster` (may live in the peer CTA).
+SP24_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                               int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+SP24_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+SP24_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+SP24_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// Arrive on the barrier at the same offset in every CTA of `mask` once the
+// pair's outstanding tcgen05 ops complete.
+SP24_DEV void tc_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+SP24_DEV void tc_cp_128x128b_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+template <int KIND>
+SP24_DEV void tc_mma_sp_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t e_tmem,
+                             uint32_t idesc, uint32_t accumulate) {
+  if constexpr (KIND == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::2.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::2.kind::f8f6f4 [%0], %1, %2, [%3], %4, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
+// 32-byte global store (one full sector per thread).
+SP24_DEV void st_global_v8(float* p, const float* v) {
+  asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v[0]), "f"(v[1]),
+               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
 }
 
 // ---------------------------------------------------------------- descriptors
