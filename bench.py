@@ -1,0 +1,455 @@
+"""Benchmark of the 2:4 sparse GEMM hot path (one JSON line on rank 0).
+
+Workload: bf16 2:4 GEMM, M = N = K = 8192, A
+U(-1,1) with a uniform 2:4 pattern per group, B dense U(-1,1), fp32
+accumulation, fp32 AND bf16 outputs.  A "step" is one GEMM (sp24_gemm, the
+C ABI) over the device-resident inputs.  With N GPUs (torchrun, one rank
+per GPU) the problem is sharded along N (north star / config 5 layout): each
+rank owns an 8192-wide column block of C, A and its metadata are replicated,
+and no collective runs on the GEMM path -> weak scaling, value = total
+dense-equivalent FLOPs of all ranks / max-over-ranks time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sp24|reference]
+                    [--config 2|3|4|5] [--allgather]
+
+Metric: dense-equivalent TFLOP/s (2MNK/t).  `roofline` compares the kernel
+with the sparse tensor peak derived from the measured dense bf16 peak
+(MEASURED_PEAKS.json) times the hardware's sparse/dense issue ratio 16/9
+(ncu: sm__ops_path_tensor_op_hmma_src_bf16_dst_fp32_sparsity_{on,off}
+.peak_sustained = 3640.9 / 2048 per cycle).  `e2e` runs the same GEMM end
+to end through sp24_gemm with host buffers: pinned H2D of A_c + reference
+metadata + B, the GEMM (metadata repack included), D2H of C.
+`cpu_baseline` / `--impl reference` time the reference's own CPU path
+(compress_structured_sparse_a + cpu_gemm_ref, compiled from its sources into
+oracle/_ref) on a bounded row sample with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "sparse-gemm-with-hopper-sptc_b200")
+sys.path.insert(0, PKG)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "2:4 GEMM dense-equiv TFLOP/s & % of sparse tensor peak at 1/2/4/8 B200"
+SPARSE_OVER_DENSE = 3640.888889 / 2048.0      # bf16/fp16 sparse vs dense issue rate
+PAIRS = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
+
+CONFIGS = {
+    2: dict(name="bf16 2:4 GEMM M=N=K=8192, fp32+bf16 out (config 2)", dt=1, m=8192, n=8192,
+            k=8192, out=("f32", "bf16"), dist="uniform"),
+    3: dict(name="e4m3 2:4 GEMM M=N=K=16384, bf16 out x 1/(sA sB) (config 3)", dt=2, m=16384,
+            n=16384, k=16384, out=("bf16",), dist="normal_fp8"),
+    4: dict(name="bf16 MLP W_up 14336x4096 x T=4096, magnitude-pruned N(0,0.02) (config 4)",
+            dt=1, m=14336, n=4096, k=4096, out=("bf16",), dist="mlp"),
+    5: dict(name="fp16 2:4 GEMM M=K=32768 per-GPU N-shard 8192 of N=65536 (config 5)", dt=0,
+            m=32768, n=8192, k=32768, out=("f32",), dist="normal"),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profile_traffic(tag):
+    """dram bytes per launch of the bench kernel, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", f"{tag}.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch"):
+            try:
+                return int(line.split("=")[1].strip().split()[0])
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = ",".join(str(g) for g in gpus)
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", self.gpus, "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(cfg, rank, torch, sp24):
+    """Device-resident A (2:4), its compression + tcgen05 metadata image, B."""
+    dev = torch.device("cuda")
+    dt, m, n, k = cfg["dt"], cfg["m"], cfg["n"], cfg["k"]
+    g = torch.Generator(device=dev).manual_seed(1234)          # A replicated on every rank
+    gb = torch.Generator(device=dev).manual_seed(4321 + rank)  # B: this rank's column block
+    tdt = {0: torch.float16, 1: torch.bfloat16, 2: torch.float8_e4m3fn}[dt]
+    scale_a = scale_b = 1.0
+    if cfg["dist"] == "mlp":
+        w = torch.randn((m, k), device=dev, generator=g) * 0.02
+        a = sp24.prune_2of4(w.to(tdt))
+        b = torch.randn((k, n), device=dev, generator=gb).to(tdt)
+    else:
+        pat = torch.randint(0, 6, (m, k // 4), device=dev, generator=g)
+        if cfg["dist"] == "uniform":
+            vals = torch.rand((m, k // 4, 2), device=dev, generator=g) * 2 - 1
+        else:
+            vals = torch.randn((m, k // 4, 2), device=dev, generator=g)
+        vals = torch.where(vals.abs() < 1e-3, torch.full_like(vals, 0.5), vals)
+        a = torch.zeros((m, k // 4, 4), device=dev)
+        a.scatter_(2, torch.tensor(PAIRS, device=dev)[pat], vals)
+        del vals, pat
+        a = a.reshape(m, k)
+        if cfg["dist"] == "uniform":
+            b = torch.rand((k, n), device=dev, generator=gb) * 2 - 1
+        else:
+            b = torch.randn((k, n), device=dev, generator=gb)
+        if dt == 2:
+            qa, sa = sp24.amax_quantize_e4m3(a)
+            qb, sb = sp24.amax_quantize_e4m3(b)
+            a, b = qa, qb
+            scale_a, scale_b = sa.item(), sb.item()
+        else:
+            a, b = a.to(tdt), b.to(tdt)
+    ac, meta = sp24.compress(a)
+    del a
+    img = sp24.repack_meta(meta, m, k, ac.dtype)
+    torch.cuda.synchronize()
+    return ac, meta, img, b, 1.0 / (scale_a * scale_b)
+
+
+def cpu_reference_rate(cfg, seconds=10.0, threads=None):
+    """The reference's CPU path (compression + cpu_gemm_ref) on a row sample of
+    the workload; returns (TFLOP/s dense-equivalent, kind, cores, sample)."""
+    import numpy as np
+    import oracle
+    threads = threads or os.cpu_count() or 1
+    dt, n, k = cfg["dt"], cfg["n"], cfg["k"]
+    rng = np.random.default_rng(7)
+    use_ref = oracle.ref_available()
+    kind = "reference" if use_ref else "port"
+
+    def sample(rows):
+        pat = rng.integers(0, 6, size=(rows, k // 4))
+        vals = rng.uniform(-1, 1, size=(rows, k // 4, 2)).astype(np.float32)
+        vals[np.abs(vals) < 1e-3] = 0.5
+        a = np.zeros((rows, k // 4, 4), np.float32)
+        np.put_along_axis(a, np.array(PAIRS)[pat], vals, axis=2)
+        return oracle.from_float(dt, a.reshape(rows, k))
+
+    b = oracle.from_float(dt, rng.uniform(-1, 1, size=(k, n)).astype(np.float32))
+
+    def run(rows):
+        a = sample(rows)
+        c = np.empty((rows, n), np.float32)
+        t0 = time.perf_counter()
+        if use_ref:
+            r = oracle.ref_lib()
+            ac = np.empty((rows, k // 2), a.dtype)
+            e = np.empty((rows, k // 8), np.uint8)
+            r.ref_compress(dt, a.ctypes.data, rows, k, ac.ctypes.data, e.ctypes.data)
+            r.ref_cpu_gemm(dt, a.ctypes.data, b.ctypes.data, c.ctypes.data, rows, n, k, threads)
+        else:
+            oracle.compress(dt, a)
+            oracle.lib().oracle_gemm(dt, a.ctypes.data, b.ctypes.data, c.ctypes.data, rows, n, k,
+                                     threads)
+        return time.perf_counter() - t0
+
+    t1 = run(threads)                       # one row per thread calibrates the rate
+    rows = max(threads, min(cfg["m"], int(threads * max(1.0, seconds / max(t1, 1e-3)))))
+    rows = (rows // threads) * threads
+    t = run(rows)
+    flops = 2.0 * rows * n * k
+    return flops / t / 1e12, kind, threads, (
+        f"{rows} of {cfg['m']} rows of A x full B ({k}x{n}), compression + fp32 CPU GEMM, "
+        f"{t:.1f} s")
+
+
+def run_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = []
+    info = None
+    for _ in range(max(1, args.warmup_ref)):
+        cpu_reference_rate(cfg, seconds=2.0)
+    for _ in range(args.steps_ref):
+        tf, kind, cores, sample = cpu_reference_rate(cfg, seconds=args.ref_seconds)
+        steps.append(tf)
+        info = (kind, cores, sample)
+    value = statistics.median(steps)
+    kind, cores, sample = info
+    flops = 2.0 * cfg["m"] * cfg["n"] * cfg["k"]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps_ref, "warmup": max(1, args.warmup_ref),
+        "ms_per_step": flops / (value * 1e12) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": {0: "f16", 1: "bf16", 2: "e4m3"}[cfg["dt"]],
+        "data": "synthetic", "config": {"workload": cfg["name"], "m": cfg["m"], "n": cfg["n"],
+                                       "k": cfg["k"], "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "reference's CPU path (its sm_90a kernels cannot run on sm_100); ms_per_step is "
+                "the full-problem time at the sampled rate",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="sp24", choices=["sp24", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--allgather", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=10.0)
+    ap.add_argument("--steps-ref", type=int, default=1)
+    ap.add_argument("--warmup-ref", type=int, default=1)
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import sp24
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if sp24.load().sp24_check_device(local) != 0:
+        raise SystemExit("sp24: device is not sm_100 — the library has no other code path")
+
+    m, n, k, dt = cfg["m"], cfg["n"], cfg["k"], cfg["dt"]
+    ac, meta, img, b, alpha = make_inputs(cfg, rank, torch, sp24)
+    dev = ac.device
+    c32 = torch.empty((m, n), dtype=torch.float32, device=dev) if "f32" in cfg["out"] else None
+    c16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev) if "bf16" in cfg["out"] else None
+    lib_dt = ac.dtype
+    desc = sp24.make_desc(ac, img, b, m, n, k, meta_format=sp24.META_TC, c_f32=c32, c_bf16=c16,
+                          alpha=alpha, dtype=lib_dt)
+    import ctypes
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    lib = sp24.load()
+
+    def step():
+        rc = lib.sp24_gemm(ctypes.byref(desc), sptr)
+        if rc != 0:
+            raise sp24.Sp24Error(rc, "sp24_gemm")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(range(torch.cuda.device_count()) if rank == 0 else [local]) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms_local = e0.elapsed_time(e1)
+    if sp24.last_kernel_status() != 0:
+        raise SystemExit("sp24: a kernel reported a bounded-wait timeout")
+    t = torch.tensor([ms_local], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = t.item()
+    ms_step = ms_total / args.steps
+    flops_rank = 2.0 * m * n * k
+    value = flops_rank * world / (ms_step * 1e-3) / 1e12
+    kernel_tflops = flops_rank / (ms_local / args.steps * 1e-3) / 1e12
+
+    # Optional replicated output: all-gather of the C shards over NVLink,
+    # timed separately from the GEMM (config 5 option).
+    allgather = None
+    if args.allgather and world > 1 and c32 is not None:
+        flat = c32.reshape(-1)
+        out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=dev)
+        dist.all_gather_into_tensor(out, flat)
+        torch.cuda.synchronize()
+        barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        dist.all_gather_into_tensor(out, flat)
+        full = sp24.unshard_columns_f32(out, m, n * world, world, n)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ta = torch.tensor([a0.elapsed_time(a1)], device=dev)
+        dist.all_reduce(ta, op=dist.ReduceOp.MAX)
+        allgather = {"ms": ta.item(), "bytes_per_rank": flat.numel() * 4 * (world - 1),
+                     "GB_per_s_per_rank": flat.numel() * 4 * (world - 1) / (ta.item() * 1e-3) / 1e9}
+        del out, full
+
+    # End to end through the public C ABI with host buffers.
+    e2e = None
+    if args.e2e_steps > 0:
+        h_ac = ac.cpu().pin_memory()
+        h_meta = meta.cpu().pin_memory()
+        h_b = b.cpu().pin_memory()
+        h_c32 = torch.empty((m, n), dtype=torch.float32).pin_memory() if c32 is not None else None
+        h_c16 = torch.empty((m, n), dtype=torch.bfloat16).pin_memory() if c16 is not None else None
+        d_ac, d_meta, d_b = torch.empty_like(ac), torch.empty_like(meta), torch.empty_like(b)
+        d2 = sp24.make_desc(d_ac, d_meta, d_b, m, n, k, meta_format=sp24.META_REF, c_f32=c32,
+                            c_bf16=c16, alpha=alpha, dtype=lib_dt)
+        ws = torch.empty(max(1, sp24.workspace_bytes(d2)), dtype=torch.uint8, device=dev)
+        d2.workspace, d2.workspace_bytes = ws.data_ptr(), ws.numel()
+
+        def e2e_step():
+            d_ac.copy_(h_ac, non_blocking=True)
+            d_meta.copy_(h_meta, non_blocking=True)
+            d_b.copy_(h_b, non_blocking=True)
+            rc = lib.sp24_gemm(ctypes.byref(d2), sptr)
+            if rc != 0:
+                raise sp24.Sp24Error(rc, "sp24_gemm")
+            if h_c32 is not None:
+                h_c32.copy_(c32, non_blocking=True)
+            if h_c16 is not None:
+                h_c16.copy_(c16, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        x0 = torch.cuda.Event(enable_timing=True)
+        x1 = torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        x1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([x0.elapsed_time(x1)], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        ms_e2e = te.item() / args.e2e_steps
+        h2d = sum(x.numel() * x.element_size() for x in (h_ac, h_meta, h_b))
+        d2h = sum(x.numel() * x.element_size() for x in (h_c32, h_c16) if x is not None)
+        e2e = {"value": flops_rank * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+               "steps": args.e2e_steps, "gpu_launches_per_step": 2}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, kind, cores, sample = cpu_reference_rate(cfg, seconds=args.ref_seconds)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": sample}
+
+    if rank == 0:
+        dense_peak, hbm_peak, peak_src = load_peaks()
+        peak_scale = 2.0 if dt == 2 else 1.0       # e4m3 issues at twice the 16-bit rate
+        sparse_peak = dense_peak * peak_scale * SPARSE_OVER_DENSE
+        out_bytes = sum(4 if o == "f32" else 2 for o in cfg["out"]) * m * n
+        esz = 1 if dt == 2 else 2
+        alg_bytes = m * k // 2 * esz + m * k // 8 + k * n * esz + out_bytes
+        tag = {2: "sp24_gemm2sm_bf16_8192", 3: "sp24_gemm2sm_e4m3_16384",
+               4: "sp24_gemm_mlp", 5: "sp24_gemm2sm_f16_32768"}[args.config]
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {0: "f16", 1: "bf16", 2: "e4m3"}[dt], "data": "synthetic",
+            "config": {"workload": cfg["name"], "m": m, "n_per_gpu": n, "n_total": n * world,
+                       "k": k, "outputs": list(cfg["out"]),
+                       "parallelism": f"N-shard x{world}, A + metadata replicated, no collective",
+                       "l2": "no flush: inputs (A_c + metadata + B) exceed the 126 MB L2"},
+            "pct_of_sparse_peak": 100.0 * kernel_tflops / sparse_peak,
+            "roofline": {"bound": "tensor", "achieved": kernel_tflops, "peak": sparse_peak,
+                         "unit": "TFLOP/s", "frac": kernel_tflops / sparse_peak,
+                         "traffic": profile_traffic(tag),
+                         "peak_basis": f"{peak_src} dense bf16 {dense_peak} TF/s x "
+                                       f"{'2 (e4m3) x ' if dt == 2 else ''}16/9 sparse issue ratio",
+                         "frac_of_nominal_sparse": kernel_tflops / (4500.0 * peak_scale),
+                         "algorithmic_bytes": alg_bytes,
+                         "hbm_GBps_at_alg_bytes": alg_bytes / (ms_local / args.steps * 1e-3) / 1e9,
+                         "hbm_peak_GBps": hbm_peak},
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        if allgather:
+            line["allgather"] = allgather
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

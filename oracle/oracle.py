@@ -1,0 +1,242 @@
+"""TEST INFRASTRUCTURE ONLY — Python face of the CPU oracle.
+
+Loads ``oracle/lib/libsp24_oracle.so`` (our C++ restatement of the
+reference's host algorithms, see sp24_oracle.cpp) and, when it was built,
+``oracle/_ref/libsp24ref.so`` (the reference's own host code compiled where
+it lies).  Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+legs use this module; the product library never does.
+
+Arrays cross as numpy raw bits: uint16 for fp16/bf16, uint8 for e4m3.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from ctypes import c_float, c_int, c_longlong, c_size_t, c_uint, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_LIB = os.path.join(HERE, "lib", "libsp24_oracle.so")
+REF_LIB = os.path.join(HERE, "_ref", "libsp24ref.so")
+
+F16, BF16, E4M3 = 0, 1, 2
+BITS = {F16: np.uint16, BF16: np.uint16, E4M3: np.uint8}
+NAMES = {"half": F16, "half_t": F16, "__nv_bfloat16": BF16, "bfloat16_t": BF16,
+         "__nv_fp8_e4m3": E4M3}
+
+_o = None
+_r = None
+
+
+def _p(a):
+    return a.ctypes.data_as(c_void_p)
+
+
+def lib():
+    global _o
+    if _o is None:
+        if not os.path.exists(ORACLE_LIB):
+            raise FileNotFoundError(f"{ORACLE_LIB} missing: run `make -C oracle`")
+        o = ctypes.CDLL(ORACLE_LIB)
+        o.oracle_gen_new.restype = c_void_p
+        o.oracle_gen_new.argtypes = [c_uint]
+        o.oracle_gen_free.argtypes = [c_void_p]
+        o.oracle_gen_structured_sparse_a.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p]
+        o.oracle_gen_pattern_sparse_a.argtypes = [c_int, c_int, c_int, c_void_p]
+        o.oracle_gen_random_b.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p]
+        o.oracle_gen_pattern_b.argtypes = [c_int, c_int, c_int, c_void_p]
+        o.oracle_compress.restype = c_longlong
+        o.oracle_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+        o.oracle_decompress.argtypes = [c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]
+        o.oracle_gemm.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int]
+        o.oracle_gemm_rows.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                       c_int, c_int]
+        o.oracle_count_abs_errors.restype = c_int
+        o.oracle_count_abs_errors.argtypes = [c_void_p, c_void_p, c_size_t, c_float]
+        o.oracle_prune_2of4.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p]
+        o.oracle_meta_tc_image.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p]
+        o.oracle_quantize_e4m3.restype = c_float
+        o.oracle_quantize_e4m3.argtypes = [c_void_p, c_size_t, c_void_p]
+        o.oracle_to_float.argtypes = [c_int, c_void_p, c_size_t, c_void_p]
+        o.oracle_from_float.argtypes = [c_int, c_void_p, c_size_t, c_void_p]
+        _o = o
+    return _o
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB)
+
+
+def ref_lib():
+    global _r
+    if _r is None:
+        if not ref_available():
+            raise FileNotFoundError(f"{REF_LIB} missing: run `make -C oracle ref`")
+        r = ctypes.CDLL(REF_LIB)
+        r.ref_gen_new.restype = c_void_p
+        r.ref_gen_new.argtypes = [c_uint]
+        r.ref_gen_free.argtypes = [c_void_p]
+        r.ref_host_case.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_void_p]
+        r.ref_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+        r.ref_cpu_gemm.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int]
+        _r = r
+    return _r
+
+
+# ------------------------------------------------------------------ generators
+class Gen:
+    """mt19937 stream shared by the cases of one suite (reference seed 1234)."""
+
+    def __init__(self, seed: int = 1234):
+        self.h = lib().oracle_gen_new(seed)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().oracle_gen_free(self.h)
+            self.h = None
+
+
+def host_case(gen: Gen, dt: int, m: int, n: int, k: int, use_pattern: bool):
+    """One case of the reference suite runner: (a_dense, b, a_c, meta, c_ref)."""
+    o = lib()
+    a = np.empty(m * k, BITS[dt])
+    b = np.empty(k * n, BITS[dt])
+    if use_pattern:
+        o.oracle_gen_pattern_sparse_a(dt, m, k, _p(a))
+        o.oracle_gen_pattern_b(dt, k, n, _p(b))
+    else:
+        o.oracle_gen_structured_sparse_a(gen.h, dt, m, k, _p(a))
+        o.oracle_gen_random_b(gen.h, dt, k, n, _p(b))
+    a_c, meta = compress(dt, a.reshape(m, k))
+    c = gemm(dt, a.reshape(m, k), b.reshape(k, n))
+    return a.reshape(m, k), b.reshape(k, n), a_c, meta, c
+
+
+def ref_host_case(rgen, dt: int, m: int, n: int, k: int, use_pattern: bool):
+    """Same as host_case, computed by the reference's own host code."""
+    r = ref_lib()
+    a = np.empty(m * k, BITS[dt])
+    b = np.empty(k * n, BITS[dt])
+    ac = np.empty(m * k // 2, BITS[dt])
+    e = np.empty(m * k // 8, np.uint8)
+    c = np.empty(m * n, np.float32)
+    r.ref_host_case(rgen, dt, m, n, k, 1 if use_pattern else 0, _p(a), _p(b), _p(ac), _p(e), _p(c))
+    return a.reshape(m, k), b.reshape(k, n), ac.reshape(m, k // 2), e.reshape(m, k // 8), c.reshape(m, n)
+
+
+# ------------------------------------------------------------------ algorithms
+def compress(dt: int, a):
+    a = np.ascontiguousarray(a)
+    m, k = a.shape
+    ac = np.empty((m, k // 2), BITS[dt])
+    meta = np.empty((m, k // 8), np.uint8)
+    bad = lib().oracle_compress(dt, _p(a), m, k, _p(ac), _p(meta))
+    if bad >= 0:
+        raise ValueError(f"not 2:4 at group {bad} (row {bad // (k // 4)}, group {bad % (k // 4)})")
+    return ac, meta
+
+
+def decompress(dt: int, a_c, meta, m: int, k: int):
+    out = np.empty((m, k), BITS[dt])
+    lib().oracle_decompress(dt, _p(np.ascontiguousarray(a_c)), _p(np.ascontiguousarray(meta)), m, k,
+                            _p(out))
+    return out
+
+
+def gemm(dt: int, a, b, threads: int = 1):
+    """fp32 sequential-k GEMM on the dense A (reference cpu_gemm_ref semantics)."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.float32)
+    lib().oracle_gemm(dt, _p(a), _p(b), _p(c), m, n, k, threads)
+    return c
+
+
+def gemm_rows(dt: int, a, b, rows):
+    """C rows for the given row indices only (sampled verification of big problems)."""
+    a = np.ascontiguousarray(a[rows])
+    return gemm(dt, a, b)
+
+
+def count_abs_errors(got, ref, atol: float = 1e-2) -> int:
+    got = np.ascontiguousarray(got, np.float32)
+    ref = np.ascontiguousarray(ref, np.float32)
+    return int(lib().oracle_count_abs_errors(_p(got), _p(ref), got.size, atol))
+
+
+def prune_2of4(dt: int, a):
+    a = np.ascontiguousarray(a)
+    out = np.empty_like(a)
+    lib().oracle_prune_2of4(dt, _p(a), a.shape[0], a.shape[1], _p(out))
+    return out
+
+
+def meta_tc_image(dt: int, meta, m: int, k: int):
+    mb = ((m + 127) // 128 + 1) // 2 * 2
+    ka = (k + 127) // 128
+    img = np.empty(mb * ka * 512, np.uint32)
+    lib().oracle_meta_tc_image(dt, _p(np.ascontiguousarray(meta)), m, k, _p(img))
+    return img.view(np.uint8)
+
+
+def quantize_e4m3(x):
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.empty(x.shape, np.uint8)
+    s = lib().oracle_quantize_e4m3(_p(x), x.size, _p(q))
+    return q, float(s)
+
+
+def to_float(dt: int, bits):
+    bits = np.ascontiguousarray(bits)
+    out = np.empty(bits.shape, np.float32)
+    lib().oracle_to_float(dt, _p(bits), bits.size, _p(out))
+    return out
+
+
+def from_float(dt: int, x):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.shape, BITS[dt])
+    lib().oracle_from_float(dt, _p(x), x.size, _p(out))
+    return out
+
+
+def row_norm_rel_error(got, ref, a_f32, b_f32) -> float:
+    """max |C - C_ref| / (||A[r,:]|| * ||B[:,n]|| / sqrt(K)) — the K-scaled
+    row-norm relative error the parity bound is stated in."""
+    k = a_f32.shape[1]
+    denom = np.outer(np.linalg.norm(a_f32, axis=1), np.linalg.norm(b_f32, axis=0)) / np.sqrt(k)
+    denom = np.maximum(denom, 1e-30)
+    return float(np.max(np.abs(np.asarray(got, np.float32) - ref) / denom))
+
+
+# ------------------------------------------------------------------ suites
+_RAW_RE = re.compile(r"RawWgmmaSparseDemo<\s*([\w:]+)\s*,\s*(\d+)\s*>")
+_CUTE_RE = re.compile(r"WgmmaSparseDemo<\s*([\w:]+)\s*,\s*[\w:]+\s*,.*?,\s*(\d+)\s*>\s*;", re.S)
+_CASE_RE = re.compile(r'\{\s*"([^"]+)"\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(true|false)\s*\}')
+_RUNCASE_RE = re.compile(r'run_case\(\s*"([^"]+)"\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(true|false)')
+
+
+def parse_entry_point(path: str):
+    """(harness, dtype, block_n, [(tag, m, n, k, pattern)]) of a reference main."""
+    src = open(path).read()
+    name = os.path.basename(path)
+    m = _RAW_RE.search(src)
+    if m:
+        harness, dt, bn = "raw", NAMES[m.group(1)], int(m.group(2))
+    else:
+        m = _CUTE_RE.search(src)
+        if m:
+            harness, dt, bn = "cute", NAMES[m.group(1)], int(m.group(2))
+        elif name == "mma_sp_wgmma_m64n8k32_fp32fp16.cu":
+            harness, dt, bn = "cute_standalone", F16, 8
+        else:
+            return None
+    cases = [(t, int(a), int(b), int(c), p == "true") for t, a, b, c, p in _CASE_RE.findall(src)]
+    if not cases:
+        cases = [(t, int(a), int(b), int(c), p == "true") for t, a, b, c, p in _RUNCASE_RE.findall(src)]
+    return harness, dt, bn, cases

@@ -56,14 +56,26 @@ void run_host_case(std::mt19937& gen, int m, int n, int k, bool use_pattern, voi
 }
 
 template <typename T>
-void gemm_rows(const void* a, const void* b, float* c, int n, int k, int r0, int r1) {
+void gemm_rows(const void* a, const std::vector<T>* bv, float* c, int n, int k, int r0, int r1) {
   // cpu_gemm_ref over a row slice: rows [r0, r1) of A against all of B.
   std::vector<T> a_rows = from_bits<T>(static_cast<const T*>(a) + static_cast<size_t>(r0) * k,
                                        static_cast<size_t>(r1 - r0) * k);
-  std::vector<T> bv = from_bits<T>(b, static_cast<size_t>(k) * n);
   std::vector<float> c_rows;
-  cpu_gemm_ref(a_rows, bv, c_rows, r1 - r0, n, k);
+  cpu_gemm_ref(a_rows, *bv, c_rows, r1 - r0, n, k);
   std::memcpy(c + static_cast<size_t>(r0) * n, c_rows.data(), c_rows.size() * sizeof(float));
+}
+
+template <typename T>
+void gemm_threads(const void* a, const void* b, float* c, int m, int n, int k, int threads) {
+  const std::vector<T> bv = from_bits<T>(b, static_cast<size_t>(k) * n);
+  const int per = (m + threads - 1) / threads;
+  std::vector<std::thread> pool;
+  for (int t = 0; t < threads; ++t) {
+    const int r0 = t * per, r1 = std::min(m, r0 + per);
+    if (r0 >= r1) break;
+    pool.emplace_back(gemm_rows<T>, a, &bv, c, n, k, r0, r1);
+  }
+  for (auto& th : pool) th.join();
 }
 
 }  // namespace
@@ -116,16 +128,9 @@ void ref_compress(int dt, const void* a, int m, int k, void* ac_out, uint8_t* e_
 void ref_cpu_gemm(int dt, const void* a, const void* b, float* c, int m, int n, int k,
                   int threads) {
   if (threads < 1) threads = 1;
-  const int per = (m + threads - 1) / threads;
-  std::vector<std::thread> pool;
-  for (int t = 0; t < threads; ++t) {
-    const int r0 = t * per, r1 = std::min(m, r0 + per);
-    if (r0 >= r1) break;
-    if (dt == 0) pool.emplace_back(gemm_rows<half>, a, b, c, n, k, r0, r1);
-    else if (dt == 1) pool.emplace_back(gemm_rows<__nv_bfloat16>, a, b, c, n, k, r0, r1);
-    else pool.emplace_back(gemm_rows<__nv_fp8_e4m3>, a, b, c, n, k, r0, r1);
-  }
-  for (auto& th : pool) th.join();
+  if (dt == 0) gemm_threads<half>(a, b, c, m, n, k, threads);
+  else if (dt == 1) gemm_threads<__nv_bfloat16>(a, b, c, m, n, k, threads);
+  else gemm_threads<__nv_fp8_e4m3>(a, b, c, m, n, k, threads);
 }
 
 }  // extern "C"

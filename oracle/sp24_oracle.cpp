@@ -189,13 +189,10 @@ void oracle_decompress(int dt, const void* a_c, const uint8_t* meta, int m, int 
 
 // ---------------------------------------------------------------- GEMM
 // c[r][n] = sum over k, in order, of float(a[r][k]) * float(b[k][n]) in fp32.
-// Rows [r0, r1) only; the threaded driver below splits rows across threads
-// and leaves the arithmetic of each element unchanged.
-void oracle_gemm_rows(int dt, const void* a, const void* b, float* c, int m, int n, int k, int r0,
-                      int r1) {
-  (void)m;
-  std::vector<float> bf(static_cast<size_t>(k) * n);
-  for (size_t i = 0; i < bf.size(); ++i) bf[i] = to_f(dt, ld(dt, b, i));
+// The threaded driver splits rows across threads and leaves the arithmetic of
+// each element unchanged; B is converted to float once and shared.
+static void gemm_rows_f(int dt, const void* a, const float* bf, float* c, int n, int k, int r0,
+                        int r1) {
   std::vector<float> arow(k);
   for (int r = r0; r < r1; ++r) {
     for (int kk = 0; kk < k; ++kk) arow[kk] = to_f(dt, ld(dt, a, static_cast<size_t>(r) * k + kk));
@@ -207,10 +204,20 @@ void oracle_gemm_rows(int dt, const void* a, const void* b, float* c, int m, int
   }
 }
 
+void oracle_gemm_rows(int dt, const void* a, const void* b, float* c, int m, int n, int k, int r0,
+                      int r1) {
+  (void)m;
+  std::vector<float> bf(static_cast<size_t>(k) * n);
+  for (size_t i = 0; i < bf.size(); ++i) bf[i] = to_f(dt, ld(dt, b, i));
+  gemm_rows_f(dt, a, bf.data(), c, n, k, r0, r1);
+}
+
 void oracle_gemm(int dt, const void* a, const void* b, float* c, int m, int n, int k,
                  int threads) {
+  std::vector<float> bf(static_cast<size_t>(k) * n);
+  for (size_t i = 0; i < bf.size(); ++i) bf[i] = to_f(dt, ld(dt, b, i));
   if (threads <= 1) {
-    oracle_gemm_rows(dt, a, b, c, m, n, k, 0, m);
+    gemm_rows_f(dt, a, bf.data(), c, n, k, 0, m);
     return;
   }
   std::vector<std::thread> pool;
@@ -218,7 +225,7 @@ void oracle_gemm(int dt, const void* a, const void* b, float* c, int m, int n, i
   for (int t = 0; t < threads; ++t) {
     const int r0 = t * per, r1 = std::min(m, r0 + per);
     if (r0 >= r1) break;
-    pool.emplace_back(oracle_gemm_rows, dt, a, b, c, m, n, k, r0, r1);
+    pool.emplace_back(gemm_rows_f, dt, a, bf.data(), c, n, k, r0, r1);
   }
   for (auto& th : pool) th.join();
 }

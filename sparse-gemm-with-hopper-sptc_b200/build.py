@@ -1,8 +1,18 @@
-"""Build recipes for the sp24 shared library (nvcc, sm_100a, in-tree output).
+"""Build recipes (nvcc, sm_100a, in-tree outputs).
 
-``python sparse-gemm-with-hopper-sptc_b200/build.py`` builds ``lib/libsp24.so``.
-The library links the CUDA runtime statically and resolves the driver's
-tensor-map encoder at run time, so it loads on a machine without a GPU.
+  build_lib()      lib/libsp24.so — the product: kernels + C ABI.  The CUDA
+                   runtime is linked statically and the driver's tensor-map
+                   encoder is resolved at run time, so the library loads on a
+                   machine without a GPU.
+  build_dropin()   bin/<entry> — the reference's own per-dtype entry points
+                   (mma_sp_wgmma_*.cu, compiled where they lie) against the
+                   drop-in headers in dropin/, linked with -lsp24.  A quoted
+                   include searches the including file's directory first, so
+                   each main is reached through a symlink in _build/dropin/
+                   that sits next to the drop-in headers.
+  build_oracle()   oracle/lib + oracle/_ref (test infrastructure, see oracle/).
+
+``python sparse-gemm-with-hopper-sptc_b200/build.py [--force]`` builds all.
 """
 from __future__ import annotations
 
@@ -47,5 +57,67 @@ def build_lib(force: bool = False) -> str:
     return out
 
 
+DROPIN = os.path.join(HERE, "dropin")
+BINDIR = os.path.join(HERE, "bin")
+REF_DIR = os.environ.get("SP24_REF_DIR", "/root/reference")
+
+
+def dropin_mains(ref_dir: str = REF_DIR):
+    """Reference entry points that include one of the two harness headers."""
+    import glob
+    out = []
+    for path in sorted(glob.glob(os.path.join(ref_dir, "mma_sp_wgmma_*.cu"))):
+        src = open(path).read()
+        if '#include "wgmma_sp_raw_common.hpp"' in src or '#include "wgmma_sp_demo_common.hpp"' in src:
+            out.append(path)
+    return out
+
+
+def build_dropin(ref_dir: str = REF_DIR, force: bool = False):
+    """Compile every reference entry point against the drop-in headers."""
+    mains = dropin_mains(ref_dir)
+    if not mains:
+        return []
+    lib = build_lib()
+    stage = os.path.join(HERE, "_build", "dropin")
+    os.makedirs(stage, exist_ok=True)
+    os.makedirs(BINDIR, exist_ok=True)
+    for h in ("wgmma_sp_raw_common.hpp", "wgmma_sp_demo_common.hpp", "sp24_host_utils.hpp"):
+        link = os.path.join(stage, h)
+        if not os.path.islink(link):
+            os.symlink(os.path.join(DROPIN, h), link)
+    deps = [lib, os.path.join(ROOT, "include", "sp24.h")] + [
+        os.path.join(DROPIN, h) for h in os.listdir(DROPIN)]
+    built = []
+    for path in mains:
+        name = os.path.basename(path)[:-3]
+        link = os.path.join(stage, name + ".cu")
+        if os.path.islink(link) and os.readlink(link) != path:
+            os.remove(link)
+        if not os.path.islink(link):
+            os.symlink(path, link)
+        out = os.path.join(BINDIR, name)
+        if force or _stale(out, deps + [path]):
+            _run([NVCC, *ARCH, "-O2", "-std=c++17", "-I" + os.path.join(ROOT, "include"), link,
+                  "-L" + LIBDIR, "-lsp24", "-Xlinker", "-rpath,$ORIGIN/../lib", "-o", out])
+        built.append(out)
+    return built
+
+
+def build_oracle(ref_dir: str = REF_DIR) -> None:
+    """CPU oracle (always) and the reference harness (when the checkout exists)."""
+    oracle_dir = os.path.join(ROOT, "oracle")
+    targets = ["oracle"]
+    if os.path.exists(os.path.join(ref_dir, "wgmma_sp_raw_common.hpp")):
+        targets.append("ref")
+    _run(["make", "-s", "-C", oracle_dir, *targets, "REF_DIR=" + ref_dir])
+
+
+def build_all(force: bool = False) -> None:
+    build_lib(force=force)
+    build_oracle()
+    build_dropin(force=force)
+
+
 if __name__ == "__main__":
-    build_lib(force="--force" in sys.argv)
+    build_all(force="--force" in sys.argv)

@@ -344,13 +344,13 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
                       int stall) {
   sp24_status st = validate(d);
   if (st != SP24_OK) return st;
-  DeviceInfo* di = nullptr;
-  st = device_info(&di);
-  if (st != SP24_OK) return st;
   const WsPlan w = plan_workspace(d);
   if (w.total > 0 && (d->workspace == nullptr || d->workspace_bytes < w.total))
     return SP24_ERR_WORKSPACE;
   if (w.total > 0 && !aligned16(d->workspace)) return SP24_ERR_ALIGN;
+  DeviceInfo* di = nullptr;
+  st = device_info(&di);
+  if (st != SP24_OK) return st;
   uint8_t* ws = static_cast<uint8_t*>(d->workspace);
 
   Prepared p{};

@@ -1,0 +1,114 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference.
+
+Run in a container that has the reference checkout (default /root/reference)
+after ``make -C oracle ref``.  For every reference entry point
+``mma_sp_wgmma_*.cu`` it parses the case table, then replays the suite exactly
+as the reference does (one mt19937 seeded 1234 shared by the cases in table
+order, wgmma_sp_raw_common.hpp:1123-1127) through the reference's own host
+code (oracle/_ref/libsp24ref.so) and records:
+
+  * sha256 of A (dense), B, A_c, the metadata bytes and C (fp32 bytes)
+  * the metadata bytes of every case, C of the pattern cases, and A/B/C of
+    the smallest random case, in golden.npz
+
+plus known-answer compressions of an alternating six-pattern matrix for each
+dtype (pins the e4m3 nibble table of wgmma_sp_raw_common.hpp:176-193).
+The CuTe harness (wgmma_sp_demo_common.hpp) shares these host algorithms;
+its suites are recorded the same way.
+
+    python tests/golden/make_golden.py [--ref-dir /root/reference]
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import oracle  # noqa: E402
+
+PAIRS = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def alternating_a(dt: int, m: int, k: int):
+    """Group g of row r keeps pair PAIRS[(r + g) % 6]; values 1 + (r + 2g + i) % 7."""
+    vals = np.zeros((m, k), np.float32)
+    for r in range(m):
+        for g in range(k // 4):
+            i0, i1 = PAIRS[(r + g) % 6]
+            vals[r, 4 * g + i0] = 1 + (r + 2 * g) % 7
+            vals[r, 4 * g + i1] = -(1 + (r + 2 * g + 1) % 7)
+    return oracle.from_float(dt, vals)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref-dir", default="/root/reference")
+    args = ap.parse_args()
+    if not oracle.ref_available():
+        sys.exit("oracle/_ref/libsp24ref.so missing: run `make -C oracle ref`")
+    r = oracle.ref_lib()
+    suites = []
+    arrays = {}
+    for path in sorted(glob.glob(os.path.join(args.ref_dir, "mma_sp_wgmma_*.cu"))):
+        parsed = oracle.parse_entry_point(path)
+        if parsed is None:
+            continue
+        harness, dt, bn, cases = parsed
+        name = os.path.basename(path)[:-3]
+        gen = r.ref_gen_new(1234)
+        rec = {"entry": name, "harness": harness, "dtype": dt, "block_n": bn, "cases": []}
+        smallest = None
+        for ci, (tag, m, n, k, pat) in enumerate(cases):
+            a, b, ac, e, c = oracle.ref_host_case(gen, dt, m, n, k, pat)
+            rec["cases"].append({"tag": tag, "m": m, "n": n, "k": k, "pattern": pat,
+                                 "sha256": {"a": sha(a), "b": sha(b), "a_c": sha(ac),
+                                            "meta": sha(e), "c": sha(c)}})
+            arrays[f"{name}/{ci}/meta"] = e
+            if pat:
+                arrays[f"{name}/{ci}/c"] = c
+            elif smallest is None or m * n * k < smallest[0]:
+                smallest = (m * n * k, ci, a, b, c)
+        r.ref_gen_free(gen)
+        _, ci, a, b, c = smallest
+        arrays[f"{name}/{ci}/a"] = a
+        arrays[f"{name}/{ci}/b"] = b
+        arrays[f"{name}/{ci}/c"] = c
+        rec["full_case"] = ci
+        suites.append(rec)
+        print(f"{name}: {harness} dt={dt} BlockN={bn} cases={len(cases)}")
+
+    kats = []
+    for dt in (oracle.F16, oracle.BF16, oracle.E4M3):
+        m, k = 128, 256
+        a = alternating_a(dt, m, k)
+        ac = np.empty((m, k // 2), oracle.BITS[dt])
+        e = np.empty((m, k // 8), np.uint8)
+        r.ref_compress(dt, a.ctypes.data, m, k, ac.ctypes.data, e.ctypes.data)
+        kats.append({"name": f"alternating6_dt{dt}", "dtype": dt, "m": m, "k": k,
+                     "sha256": {"a": sha(a), "a_c": sha(ac), "meta": sha(e)}})
+        arrays[f"kat/alternating6_dt{dt}/meta"] = e
+        arrays[f"kat/alternating6_dt{dt}/a_c"] = ac
+
+    out = {"generator": "tests/golden/make_golden.py", "reference_seed": 1234,
+           "suites": suites, "kats": kats}
+    with open(os.path.join(HERE, "golden.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)
+    size = os.path.getsize(os.path.join(HERE, "golden.npz"))
+    print(f"wrote golden.json ({len(suites)} suites) and golden.npz ({size / 1024:.0f} KiB)")
+
+
+if __name__ == "__main__":
+    main()

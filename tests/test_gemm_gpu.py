@@ -1,0 +1,356 @@
+"""GPU parity of the sp24 kernels against the CPU oracle (itself pinned to
+the reference's outputs by test_oracle.py).  Every call goes through the C
+ABI (sp24.py is a ctypes shim over lib/libsp24.so).
+
+Tolerances, as the reference and the north star state them:
+  * the reference's own rule: |C - C_ref| <= 1e-2 per element, zero errors
+    (wgmma_sp_raw_common.hpp:227-248);
+  * relative to K-scaled row norms, max |C - C_ref| / (|A_r| |B_n| / sqrt(K)):
+    <= 1e-2 for fp16/bf16, <= 2e-2 for e4m3 (the stated looser bound);
+  * compressed values, metadata, metadata images, pruning and e4m3
+    quantisation: bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import sp24
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+TOL = {0: 1e-2, 1: 1e-2, 2: 2e-2}
+PAIRS = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
+
+
+def to_dev(bits, dt):
+    if bits.dtype == np.uint16:
+        t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16))
+        return t.view(torch.float16 if dt == 0 else torch.bfloat16).to(DEV)
+    return torch.from_numpy(np.ascontiguousarray(bits)).to(DEV)
+
+
+def to_host_bits(t):
+    if t.dtype in (torch.float16, torch.bfloat16):
+        return t.cpu().view(torch.int16).numpy().view(np.uint16)
+    return t.cpu().numpy()
+
+
+def lib_dtype(dt):
+    return {0: torch.float16, 1: torch.bfloat16, 2: torch.uint8}[dt]
+
+
+def check_c(c_gpu, c_ref, a_bits, b_bits, dt, abs_rule=True):
+    c = c_gpu.cpu().numpy()
+    if abs_rule:
+        assert oracle.count_abs_errors(c, c_ref, 1e-2) == 0
+    err = oracle.row_norm_rel_error(c, c_ref, oracle.to_float(dt, a_bits), oracle.to_float(dt, b_bits))
+    assert err <= TOL[dt], err
+
+
+@pytest.fixture(autouse=True)
+def _clean_status():
+    yield
+    assert sp24.last_kernel_status() == 0, "a kernel raised its bounded-wait timeout flag"
+
+
+# ------------------------------------------------------------------ reference suites
+@pytest.mark.parametrize("suite_idx", range(24))
+def test_reference_suite(golden, suite_idx):
+    """Every case of every reference entry point, through the same seeded
+    stream: GPU compression bit-exact, C within the reference's abs 1e-2
+    rule and the row-norm bound, on the entry point's own tile width, with
+    reference-layout metadata (repacked on the fly) and with the tcgen05
+    image (identical C)."""
+    meta, arrays = golden
+    suite = meta["suites"][suite_idx]
+    dt, bn = suite["dtype"], suite["block_n"]
+    gen = oracle.Gen(1234)
+    for ci, case in enumerate(suite["cases"]):
+        m, n, k = case["m"], case["n"], case["k"]
+        a, b, a_c, e, c_ref = oracle.host_case(gen, dt, m, n, k, case["pattern"])
+        ac_t, e_t = sp24.compress(to_dev(a, dt))
+        np.testing.assert_array_equal(to_host_bits(ac_t), a_c)
+        np.testing.assert_array_equal(e_t.cpu().numpy(), e)
+        np.testing.assert_array_equal(e_t.cpu().numpy(), arrays[f"{suite['entry']}/{ci}/meta"])
+        b_t = to_dev(b, dt)
+        c1, _ = sp24.gemm(ac_t, e_t, b_t, m, n, k, tile_n=bn, dtype=lib_dtype(dt))
+        check_c(c1, c_ref, a, b, dt)
+        img = sp24.repack_meta(e_t, m, k, lib_dtype(dt))
+        c2, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC, tile_n=bn,
+                          dtype=lib_dtype(dt))
+        torch.cuda.synchronize()
+        assert torch.equal(c1, c2)
+        if f"{suite['entry']}/{ci}/c" in arrays.files:
+            np.testing.assert_array_equal(c_ref, arrays[f"{suite['entry']}/{ci}/c"])
+
+
+# ------------------------------------------------------------------ bit-exact prep kernels
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,k", [(64, 64), (200, 384), (256, 1024), (1000, 2048)])
+def test_repack_matches_oracle_image(dt, m, k):
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    gen = oracle.Gen(3)
+    _, _, _, e, _ = oracle.host_case(gen, dt, m, 8, k, False)
+    img = sp24.repack_meta(to_dev(e, dt), m, k, lib_dtype(dt))
+    np.testing.assert_array_equal(img.cpu().numpy(), oracle.meta_tc_image(dt, e, m, k))
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_prune_matches_oracle(dt):
+    rng = np.random.default_rng(dt)
+    x = oracle.from_float(dt, (rng.standard_normal((256, 512)) * 0.02).astype(np.float32))
+    x[0, :4] = oracle.from_float(dt, np.array([1, 1, 1, 1], np.float32))     # ties
+    got = to_host_bits(sp24.prune_2of4(to_dev(x, dt)))
+    np.testing.assert_array_equal(got, oracle.prune_2of4(dt, x))
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_compress_reports_first_bad_group(dt):
+    gen = oracle.Gen(4)
+    a, *_ = oracle.host_case(gen, dt, 64, 8, 128, False)
+    a = a.copy()
+    a[37, 4 * 5: 4 * 6] = 0            # row 37, group 5 -> no nonzero
+    a[50, 0: 4] = a[50, 0]             # later bad group must not win
+    with pytest.raises(sp24.Sp24Error) as ei:
+        sp24.compress(to_dev(a, dt))
+    assert ei.value.code == 3
+    assert ei.value.bad_group == 37 * (128 // 4) + 5
+
+
+# ------------------------------------------------------------------ known-answer tests
+def _decode_case(dt, m, k, seed):
+    """A_c values 1..7 (exact in every type) under random 2:4 patterns."""
+    rng = np.random.default_rng(seed)
+    pat = rng.integers(0, 6, size=(m, k // 4))
+    vals = (np.arange(m * (k // 4) * 2).reshape(m, k // 4, 2) % 7 + 1).astype(np.float32)
+    a = np.zeros((m, k // 4, 4), np.float32)
+    idx = np.array(PAIRS)[pat]
+    np.put_along_axis(a, idx, vals, axis=2)
+    return oracle.from_float(dt, a.reshape(m, k))
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("kernel,bn,m", [("1sm", 16, 128), ("1sm", 32, 128), ("1sm", 64, 128),
+                                         ("1sm", 128, 128), ("1sm", 256, 128),
+                                         ("2sm", 256, 256), ("2sm", 256, 512)])
+def test_decode_known_answer(dt, kernel, bn, m, monkeypatch):
+    """B = identity: C must equal the dense A exactly, so every metadata
+    nibble, lane and column of the TMEM image is checked."""
+    monkeypatch.setenv("SP24_KERNEL", kernel)
+    k = 256
+    n = max(k, bn)
+    a = _decode_case(dt, m, k, seed=bn + m)
+    b = oracle.from_float(dt, np.eye(k, n, dtype=np.float32))
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    c, _ = sp24.gemm(ac_t, e_t, to_dev(b, dt), m, n, k, tile_n=bn, dtype=lib_dtype(dt))
+    expect = np.zeros((m, n), np.float32)
+    expect[:, :k] = oracle.to_float(dt, a)
+    np.testing.assert_array_equal(c.cpu().numpy(), expect)
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_one_hot_b_every_k_position(dt):
+    """One-hot B columns select single dense-K positions (each of the four
+    in-group positions, every group): C[:, j] = A[:, pos(j)]."""
+    m, k = 128, 256
+    n = k
+    a = _decode_case(dt, m, k, seed=17)
+    perm = np.random.default_rng(5).permutation(k)
+    bf = np.zeros((k, n), np.float32)
+    bf[perm, np.arange(n)] = 1.0
+    b = oracle.from_float(dt, bf)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    c, _ = sp24.gemm(ac_t, e_t, to_dev(b, dt), m, n, k, dtype=lib_dtype(dt))
+    np.testing.assert_array_equal(c.cpu().numpy(), oracle.to_float(dt, a)[:, perm])
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("kernel", ["1sm", "2sm"])
+def test_alternating_six_pattern(dt, kernel, monkeypatch):
+    """The reference debugging log's signature of a wrong metadata layout is
+    'one-hot passes, alternating fails'; the alternating six-pattern A is
+    checked against the oracle with random B."""
+    from tests.golden.make_golden import alternating_a
+    monkeypatch.setenv("SP24_KERNEL", kernel)
+    m, n, k = 256, 256, 512
+    a = alternating_a(dt, m, k)
+    rng = np.random.default_rng(9)
+    b = oracle.from_float(dt, rng.uniform(-1, 1, (k, n)).astype(np.float32))
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    c, _ = sp24.gemm(ac_t, e_t, to_dev(b, dt), m, n, k, dtype=lib_dtype(dt))
+    check_c(c, oracle.gemm(dt, a, b), a, b, dt, abs_rule=False)
+
+
+# ------------------------------------------------------------------ random shapes
+SHAPES = [(64, 8, 32), (64, 16, 64), (128, 24, 96), (192, 40, 128), (320, 300, 256),
+          (256, 256, 64), (384, 640, 1024), (1000, 1000, 512), (512, 768, 2048),
+          (4096, 16, 4096), (1, 17, 128), (129, 255, 320)]
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_random_shapes(dt, m, n, k):
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    gen = oracle.Gen(m * 7 + n + k)
+    a, b, a_c, e, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    c, cb = sp24.gemm(ac_t, e_t, to_dev(b, dt), m, n, k, out_bf16=True, dtype=lib_dtype(dt))
+    check_c(c, c_ref, a, b, dt, abs_rule=(k <= 512))
+    # the bf16 output is the round-to-nearest-even of the fp32 output
+    assert torch.equal(cb, c.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_alpha_and_strided_output(dt):
+    """alpha scaling and a C row pitch wider than N (scalar store path)."""
+    gen = oracle.Gen(21)
+    m, n, k = 256, 192, 256
+    a, b, _, _, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    big = torch.full((m, n + 3), -1.0, device=DEV)
+    view = big[:, :n]
+    sp24.gemm(ac_t, e_t, to_dev(b, dt), m, n, k, c_f32=view, alpha=0.5, dtype=lib_dtype(dt))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(view.cpu().numpy(), 0.5 * c_ref, rtol=0, atol=1e-2)
+    assert (big[:, n:] == -1.0).all()
+
+
+def test_kernels_agree():
+    """The single-CTA and CTA-pair kernels run the same K order per output."""
+    gen = oracle.Gen(8)
+    m, n, k = 512, 512, 1024
+    a, b, *_ = oracle.host_case(gen, 1, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, 1))
+    b_t = to_dev(b, 1)
+    old = os.environ.get("SP24_KERNEL")
+    try:
+        os.environ["SP24_KERNEL"] = "1sm"
+        c1, _ = sp24.gemm(ac_t, e_t, b_t, m, n, k, tile_n=256)
+        os.environ["SP24_KERNEL"] = "2sm"
+        c2, _ = sp24.gemm(ac_t, e_t, b_t, m, n, k)
+        torch.cuda.synchronize()
+    finally:
+        if old is None:
+            os.environ.pop("SP24_KERNEL", None)
+        else:
+            os.environ["SP24_KERNEL"] = old
+    assert (c1 - c2).abs().max().item() <= 1e-5
+
+
+# ------------------------------------------------------------------ e4m3 configuration
+def test_e4m3_quantize_and_scaled_gemm():
+    """Benchmark configuration 3 at a small size: A, B ~ N(0,1) scaled by
+    448/amax and rounded to e4m3 on the GPU (bit-exact vs the oracle), A
+    2:4-pruned, C = (A_q B_q) / (s_A s_B) checked on the dequantised values."""
+    rng = np.random.default_rng(3)
+    m, n, k = 512, 512, 1024
+    af = rng.standard_normal((m, k)).astype(np.float32)
+    bf = rng.standard_normal((k, n)).astype(np.float32)
+    qa, sa = sp24.amax_quantize_e4m3(torch.from_numpy(af).to(DEV))
+    qb, sb = sp24.amax_quantize_e4m3(torch.from_numpy(bf).to(DEV))
+    qa_ref, sa_ref = oracle.quantize_e4m3(af)
+    qb_ref, sb_ref = oracle.quantize_e4m3(bf)
+    np.testing.assert_array_equal(qa.cpu().numpy(), qa_ref)
+    np.testing.assert_array_equal(qb.cpu().numpy(), qb_ref)
+    assert sa.item() == pytest.approx(sa_ref) and sb.item() == pytest.approx(sb_ref)
+    qa_p = sp24.prune_2of4(qa)
+    ac_t, e_t = sp24.compress(qa_p)
+    alpha = 1.0 / (sa.item() * sb.item())
+    c, cb = sp24.gemm(ac_t, e_t, qb, m, n, k, alpha=alpha, out_bf16=True, dtype=torch.uint8)
+    a_deq = oracle.to_float(2, qa_p.cpu().numpy()) / sa_ref
+    b_deq = oracle.to_float(2, qb_ref) / sb_ref
+    ref = a_deq @ b_deq
+    err = oracle.row_norm_rel_error(cb.float().cpu().numpy(), ref, a_deq, b_deq)
+    assert err <= TOL[2], err
+
+
+# ------------------------------------------------------------------ full-size properties
+def test_config2_bf16_8192_sampled_rows():
+    """Benchmark configuration 2 at full size (bf16 8192^3, U(-1,1), uniform
+    2:4 pattern): GPU compression bit-exact on the whole matrix, C (fp32 and
+    bf16) checked on 64 seeded rows against the oracle's fp32 GEMM."""
+    g = torch.Generator(device=DEV).manual_seed(2)
+    m = n = k = 8192
+    pat = torch.randint(0, 6, (m, k // 4), device=DEV, generator=g)
+    vals = torch.rand((m, k // 4, 2), device=DEV, generator=g) * 2 - 1
+    vals = torch.where(vals.abs() < 1e-3, torch.full_like(vals, 0.5), vals)
+    a = torch.zeros((m, k // 4, 4), device=DEV)
+    a.scatter_(2, torch.tensor(PAIRS, device=DEV)[pat], vals)
+    a = a.reshape(m, k).to(torch.bfloat16)
+    b = (torch.rand((k, n), device=DEV, generator=g) * 2 - 1).to(torch.bfloat16)
+    ac_t, e_t = sp24.compress(a)
+    a_bits = to_host_bits(a)
+    a_c_ref, e_ref = oracle.compress(1, a_bits)
+    np.testing.assert_array_equal(e_t.cpu().numpy(), e_ref)
+    np.testing.assert_array_equal(to_host_bits(ac_t), a_c_ref)
+    img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
+    c, cb = sp24.gemm(ac_t, img, b, m, n, k, meta_format=sp24.META_TC, out_bf16=True)
+    torch.cuda.synchronize()
+    rows = np.sort(np.random.default_rng(2).choice(m, 64, replace=False))
+    b_bits = to_host_bits(b)
+    ref = oracle.gemm(1, a_bits[rows], b_bits, threads=8)
+    af, bf = oracle.to_float(1, a_bits[rows]), oracle.to_float(1, b_bits)
+    assert oracle.row_norm_rel_error(c[rows].cpu().numpy(), ref, af, bf) <= 1e-2
+    assert oracle.row_norm_rel_error(cb[rows].float().cpu().numpy(), ref, af, bf) <= 1e-2
+    # column checksum of the whole product against an fp32 torch reference
+    ones = torch.ones((n, 1), device=DEV)
+    lhs = (c @ ones).squeeze(1)
+    rhs = (a.float() @ (b.float() @ ones)).squeeze(1)
+    assert ((lhs - rhs).abs() / (rhs.abs() + 1e2)).max().item() < 1e-3
+
+
+# ------------------------------------------------------------------ sharding and failure paths
+def test_nshard_on_one_gpu_matches_full():
+    """Configuration 5's N-sharding, emulated rank by rank on one GPU: each
+    shard multiplies a strided column view of B into its own packed block;
+    the packed blocks, unsharded by the library kernel, equal the full GEMM."""
+    gen = oracle.Gen(12)
+    m, n, k, world = 512, 1280, 512, 4
+    a, b, *_ = oracle.host_case(gen, 0, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, 0))
+    img = sp24.repack_meta(e_t, m, k, torch.float16)
+    b_t = to_dev(b, 0)
+    full, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC)
+    blocks = []
+    for r in range(world):
+        n0, n1 = sp24.shard_columns(n, world, r, 256)
+        if n1 == n0:
+            continue   # more ranks than 256-wide column blocks: this rank idles
+        c_r, _ = sp24.gemm(ac_t, img, b_t[:, n0:n1], m, n1 - n0, k, meta_format=sp24.META_TC)
+        blocks.append(c_r.reshape(-1))
+    packed = torch.cat(blocks)
+    rebuilt = sp24.unshard_columns_f32(packed, m, n, world, 256)
+    torch.cuda.synchronize()
+    assert torch.equal(rebuilt, full)
+
+
+def test_bounded_wait_timeout_returns_error_and_context_survives():
+    """A producer that never loads: the MMA / epilogue waits run out after
+    2 ms, the kernel frees its TMEM and returns; the status word says so and
+    the next GEMM on the same context is correct."""
+    import ctypes
+    gen = oracle.Gen(13)
+    for kernel, (m, n, k) in (("1sm", (128, 128, 256)), ("2sm", (256, 256, 256))):
+        a, b, _, _, c_ref = oracle.host_case(gen, 1, m, n, k, False)
+        ac_t, e_t = sp24.compress(to_dev(a, 1))
+        img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
+        b_t = to_dev(b, 1)
+        c = torch.zeros((m, n), device=DEV)
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        d = sp24.make_desc(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC, c_f32=c,
+                           status=status)
+        os.environ["SP24_KERNEL"] = kernel
+        try:
+            rc = sp24.load().sp24_selftest_timeout(ctypes.byref(d), 2_000_000,
+                                                   torch.cuda.current_stream().cuda_stream)
+        finally:
+            os.environ.pop("SP24_KERNEL", None)
+        assert rc == 6
+        c2, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC)
+        check_c(c2, c_ref, a, b, 1)

@@ -1,0 +1,158 @@
+"""The CPU oracle pinned against the reference's own outputs (golden vectors
+recorded from wgmma_sp_raw_common.hpp's host code, tests/golden/), plus the
+properties of the functions that have no reference counterpart."""
+import hashlib
+
+import numpy as np
+import pytest
+
+import oracle
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_golden_covers_every_entry_point(golden):
+    meta, _ = golden
+    names = {s["entry"] for s in meta["suites"]}
+    assert len([n for n in names if n.startswith("mma_sp_wgmma_cuda_")]) == 18
+    assert len([n for n in names if not n.startswith("mma_sp_wgmma_cuda_")]) == 6
+    assert sum(len(s["cases"]) for s in meta["suites"]) == 72
+
+
+@pytest.mark.parametrize("suite_idx", range(24))
+def test_oracle_replays_reference_suite_bit_exact(golden, suite_idx):
+    """Generation (mt19937 call order), compression and the fp32 CPU GEMM
+    reproduce the reference bit for bit, case by case, in suite order."""
+    meta, arrays = golden
+    suite = meta["suites"][suite_idx]
+    gen = oracle.Gen(1234)
+    for ci, case in enumerate(suite["cases"]):
+        a, b, a_c, e, c = oracle.host_case(gen, suite["dtype"], case["m"], case["n"], case["k"],
+                                           case["pattern"])
+        h = case["sha256"]
+        assert sha(a) == h["a"], (suite["entry"], case["tag"], "A")
+        assert sha(b) == h["b"], (suite["entry"], case["tag"], "B")
+        assert sha(a_c) == h["a_c"], (suite["entry"], case["tag"], "A_c")
+        assert sha(e) == h["meta"], (suite["entry"], case["tag"], "metadata")
+        assert sha(c) == h["c"], (suite["entry"], case["tag"], "C")
+        np.testing.assert_array_equal(e, arrays[f"{suite['entry']}/{ci}/meta"])
+
+
+def test_alternating_kats_bit_exact(golden):
+    """Alternating six-pattern A (the adversarial metadata case): compressed
+    values and metadata equal the reference's, for fp16, bf16 and e4m3 (the
+    e4m3 path of the reference uses its own nibble table)."""
+    meta, arrays = golden
+    from tests.golden.make_golden import alternating_a
+    for kat in meta["kats"]:
+        a = alternating_a(kat["dtype"], kat["m"], kat["k"])
+        assert sha(a) == kat["sha256"]["a"]
+        a_c, e = oracle.compress(kat["dtype"], a)
+        np.testing.assert_array_equal(e, arrays[f"kat/{kat['name']}/meta"])
+        np.testing.assert_array_equal(a_c, arrays[f"kat/{kat['name']}/a_c"])
+
+
+def test_e4m3_nibble_table_equals_generic_code():
+    """The reference's e4m3 table maps (0,1)->4 (1,2)->9 (2,3)->E (0,2)->8
+    (1,3)->D (0,3)->C: exactly i0 | i1 << 2."""
+    table = {(0, 1): 0x4, (1, 2): 0x9, (2, 3): 0xE, (0, 2): 0x8, (1, 3): 0xD, (0, 3): 0xC}
+    for (i0, i1), code in table.items():
+        assert i0 | (i1 << 2) == code
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference harness not built here")
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_oracle_matches_reference_on_fresh_seeds(dt):
+    """Beyond the golden tables: other seeds and shapes, oracle vs the
+    reference's compiled host code."""
+    r = oracle.ref_lib()
+    # The pattern A has an exact zero at group 32 + 4*row (-0.5 + 0.015625*32),
+    # which the reference rejects, so pattern cases stay at k <= 128.
+    for seed, (m, n, k), patterns in ((7, (64, 48, 128), (False, True, False)),
+                                      (99, (192, 40, 256), (False, False))):
+        rg = r.ref_gen_new(seed)
+        og = oracle.Gen(seed)
+        for pattern in patterns:
+            ref = oracle.ref_host_case(rg, dt, m, n, k, pattern)
+            got = oracle.host_case(og, dt, m, n, k, pattern)
+            for x, y in zip(got, ref):
+                np.testing.assert_array_equal(x, y)
+        r.ref_gen_free(rg)
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_decompress_inverts_compress(dt):
+    gen = oracle.Gen(5)
+    a, _, a_c, e, _ = oracle.host_case(gen, dt, 32, 8, 64, False)
+    np.testing.assert_array_equal(oracle.decompress(dt, a_c, e, 32, 64), a)
+
+
+def test_compress_rejects_non_2of4():
+    a = oracle.from_float(0, np.ones((4, 8), np.float32))
+    with pytest.raises(ValueError):
+        oracle.compress(0, a)
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_prune_keeps_two_largest_ties_low(dt):
+    x = np.array([[0.5, -2.0, 1.0, 3.0, 1.0, 1.0, 1.0, 1.0, 0.0, 0.0, 0.0, -0.25]], np.float32)
+    p = oracle.to_float(dt, oracle.prune_2of4(dt, oracle.from_float(dt, x)))
+    np.testing.assert_array_equal(p[0, :4] != 0, [False, True, False, True])
+    np.testing.assert_array_equal(p[0, 4:8] != 0, [True, True, False, False])   # tie -> low idx
+    np.testing.assert_array_equal(p[0, 8:12] != 0, [False, False, False, True])
+    rng = np.random.default_rng(0)
+    y = oracle.from_float(dt, rng.standard_normal((16, 64)).astype(np.float32))
+    py = oracle.to_float(dt, oracle.prune_2of4(dt, y)).reshape(16, 16, 4)
+    assert ((py != 0).sum(-1) <= 2).all()
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+def test_meta_tc_image_layout(dt):
+    """tcgen05 image: e4m3 lanes are rows with the row's reference bytes;
+    16-bit lanes interleave rows r / r+8 per 16-bit half; padding code 0x4."""
+    gen = oracle.Gen(11)
+    m, k = 200, 384 if dt != 2 else 384
+    _, _, _, e, _ = oracle.host_case(gen, dt, m, 8, k, False)
+    img = oracle.meta_tc_image(dt, e, m, k)
+    mb = ((m + 127) // 128 + 1) // 2 * 2
+    ka = (k + 127) // 128
+    assert img.size == mb * ka * 2048
+    words = img.view(np.uint32).reshape(ka, mb, 128, 4)
+    rb = k // 8
+    for (kk, b_, lane, w) in ((0, 0, 0, 0), (1, 1, 37, 3), (2, 0, 127, 2), (2, 1, 71, 1)):
+        if dt == 2:
+            row = b_ * 128 + lane
+            want = (int.from_bytes(e[row, kk * 16 + 4 * w: kk * 16 + 4 * w + 4].tobytes(), "little")
+                    if row < m else 0x44444444)
+        else:
+            m2, k1, m0 = lane // 16, (lane // 8) % 2, lane % 8
+            kr = kk * 128 + 32 * w + 16 * k1
+            want = 0
+            for h in (0, 1):
+                row = b_ * 128 + 16 * m2 + 8 * h + m0
+                half = (int.from_bytes(e[row, kr // 8: kr // 8 + 2].tobytes(), "little")
+                        if row < m else 0x4444)
+                want |= half << (16 * h)
+        assert int(words[kk, b_, lane, w]) == want
+    assert (words[:, 2:, :, :] == 0x44444444).all()  # padding rows of the even-block pad
+
+
+def test_quantize_e4m3_scale():
+    x = np.array([0.5, -2.0, 1.0, 0.001], np.float32)
+    q, s = oracle.quantize_e4m3(x)
+    assert s == pytest.approx(448.0 / 2.0)
+    assert q[1] == 0xFE   # -448 in e4m3
+    back = oracle.to_float(2, q) / s
+    np.testing.assert_allclose(back[:3], x[:3], rtol=1 / 16)
+
+
+def test_abs_error_count_and_row_norm_metric():
+    ref = np.zeros((2, 3), np.float32)
+    got = ref.copy()
+    got[0, 1] = 0.02
+    assert oracle.count_abs_errors(got, ref, 1e-2) == 1
+    a = np.ones((2, 4), np.float32)
+    b = np.ones((4, 3), np.float32)
+    assert oracle.row_norm_rel_error(got, ref, a, b) == pytest.approx(0.02 / (2 * 2 / 2))
