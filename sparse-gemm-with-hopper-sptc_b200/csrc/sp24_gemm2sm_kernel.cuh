@@ -88,6 +88,7 @@ struct PairCfg {
   static constexpr uint32_t IDESC = make_idesc_sparse(FMT, 256, 256, true);
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
+  static_assert(MMAS == 4, "full stages are issued as one block of four MMAs");
   static_assert(LOADS <= 32, "one lane per TMA box");
 };
 
@@ -276,29 +277,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
+    // The whole warp runs this loop converged (all operands warp-uniform);
+    // tcgen05 instructions are issued by one elected lane inside the asm.
     // Descriptors are formed once; per stage only the start-address field
     // moves (stage offset >> 4 added to the 64-bit descriptor), per MMA by a
     // compile-time step.  Metadata: atom a of a stage lives in TMEM columns
     // E_COL + ebuf*ATOMS*4 + a*4; kind::f16 MMAs use one column each (odd
     // columns through the sparsity selector), kind::f8f6f4 MMAs two.
-    if (leader && lane == 0) {
+    if (leader) {
       const uint32_t smem_base = smem_u32(smem);
       const uint64_t adesc0 = make_sdesc(smem_base, 16, 1024, kLayoutSW128);
       const uint64_t bdesc0 = make_sdesc(smem_base + C::A_BYTES, C::B_LBO, C::B_SBO, kLayoutSW128);
       const uint64_t edesc0 =
           make_sdesc(smem_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
       constexpr uint32_t SD = C::STAGE_BYTES >> 4;
+      constexpr int kPerAtom = 128 / C::MMA_K;
+      // Per-MMA constants: metadata column offset and sparsity selector.
+      uint32_t ecol[C::MMAS], isel[C::MMAS];
+#pragma unroll
+      for (int j = 0; j < C::MMAS; ++j) {
+        const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(j % kPerAtom)
+                                            : static_cast<uint32_t>(2 * (j % kPerAtom));
+        ecol[j] = 4u * static_cast<uint32_t>(j / kPerAtom) + (col & ~1u);
+        isel[j] = C::IDESC | (col & 1u);
+      }
       int s = 0;
       uint32_t ph = 0, soff = 0, aph = 0, ebuf = 0;
       bool ok = true, any = false;
       for (int t = pair; t < P.num_tiles && ok; t += npairs) {
-        if (!mbar_wait_fast<true>(&acce_bar, aph ^ 1u, &abort_sh, tmo)) {
+        if (!mbar_wait_warp<true>(&acce_bar, aph ^ 1u, &abort_sh, tmo)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int ks = 0; ks < P.k_stages; ++ks) {
-          if (!mbar_wait_fast(&full_bar[s], ph, &abort_sh, tmo)) {
+          if (!mbar_wait_warp(&full_bar[s], ph, &abort_sh, tmo)) {
             ok = false;
             break;
           }
@@ -306,36 +319,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
 #pragma unroll
           for (int a = 0; a < C::ATOMS; ++a)
-            tc_cp_128x128b_pair(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
+            tc_cp_elect<2>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
           const int kleft = P.k - ks * C::BKD;
           const uint32_t acc0 = ks > 0 ? 1u : 0u;
+          uint64_t ad[C::MMAS], bd[C::MMAS];
+          uint32_t ed[C::MMAS];
 #pragma unroll
           for (int j = 0; j < C::MMAS; ++j) {
-            if (j * C::MMA_K < kleft) {
-              constexpr int kPerAtom = 128 / C::MMA_K;
-              const int a = j / kPerAtom;
-              const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(j % kPerAtom)
-                                                  : static_cast<uint32_t>(2 * (j % kPerAtom));
-              const uint32_t eaddr = e_tmem + 4u * a + (col & ~1u);
-              tc_mma_sp_pair<C::KIND>(tmem_base, adesc0 + soff + j * 2,
-                                      bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4), eaddr,
-                                      C::IDESC | (col & 1u), j > 0 ? 1u : acc0);
-            }
+            ad[j] = adesc0 + soff + j * 2;
+            bd[j] = bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4);
+            ed[j] = e_tmem + ecol[j];
+          }
+          if (kleft >= C::BKD) {
+            tc_mma_sp_elect_x4<2, C::KIND>(tmem_base, ad, bd, ed, isel, acc0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < C::MMAS; ++j)
+              if (j * C::MMA_K < kleft)
+                tc_mma_sp_elect<2, C::KIND>(tmem_base, ad[j], bd[j], ed[j], isel[j],
+                                            j > 0 ? 1u : acc0);
           }
           any = true;
-          tc_commit_pair(&empty_bar[s], static_cast<uint16_t>(3));
+          tc_commit_elect<2>(&empty_bar[s], static_cast<uint16_t>(3));
           ebuf ^= static_cast<uint32_t>(C::ATOMS * 4);
           soff += SD;
           if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
         if (!ok) break;
-        tc_commit_pair(&accf_bar, static_cast<uint16_t>(3));
+        tc_commit_elect<2>(&accf_bar, static_cast<uint16_t>(3));
         aph ^= 1u;
       }
       if (!ok && any) {
         volatile int dummy = 0;
-        tc_commit_pair(&drain_bar, static_cast<uint16_t>(1));
-        mbar_wait(&drain_bar, 0, &dummy, tmo);
+        tc_commit_elect<2>(&drain_bar, static_cast<uint16_t>(1));
+        if (lane == 0) mbar_wait(&drain_bar, 0, &dummy, tmo);
+        __syncwarp();
       }
     }
   } else {

@@ -103,6 +103,7 @@ struct GemmCfg {
   static_assert(BN % B_BOXN == 0, "B tile must be whole TMA boxes");
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
+  static_assert(MMAS == 2, "a full stage is issued as one block of two MMAs");
 };
 
 SP24_DEV void tile_coords(const GemmParams& P, int t, int& mb, int& nb) {
@@ -254,71 +255,77 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // Converged warp loop; tcgen05 instructions issued by an elected lane.
+    {
+      const uint32_t a_base = smem_u32(smem);
+      const uint64_t adesc0 = make_sdesc(a_base, 16, 512, kLayoutSW64);
+      const uint64_t bdesc0 = make_sdesc(a_base + C::A_BYTES, C::B_LBO, C::B_SBO, C::B_LAYOUT);
+      const uint64_t edesc0 =
+          make_sdesc(a_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
+      constexpr uint32_t SD = C::STAGE_BYTES >> 4;
       int s = 0;
-      uint32_t ph = 0;
+      uint32_t ph = 0, soff = 0;
       int ab = 0;
       uint32_t aph = 0;
       bool ok = true;
       bool any_issued = false;
-      const uint32_t a_base = smem_u32(smem);
       for (int t = blockIdx.x; t < P.num_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&acce_bar[ab], aph ^ 1u, &abort_sh, tmo)) {
+        if (!mbar_wait_warp(&acce_bar[ab], aph ^ 1u, &abort_sh, tmo)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * BN);
         for (int ks = 0; ks < P.k_stages; ++ks) {
-          if (!mbar_wait(&full_bar[s], ph, &abort_sh, tmo)) {
+          if (!mbar_wait_warp(&full_bar[s], ph, &abort_sh, tmo)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = a_base + static_cast<uint32_t>(s * C::STAGE_BYTES);
           const int sub = ks % C::STAGES_PER_ATOM;
           const uint32_t e_tmem =
               tmem_base + static_cast<uint32_t>(C::E_COL + ((ks / C::STAGES_PER_ATOM) & 1) * 4);
-          if (sub == 0) {
-            // Metadata atom: 128 rows of 16 B, rows contiguous -> K-major
-            // no-swizzle canonical layout, 8-row groups 128 B apart.
-            const uint64_t edesc =
-                make_sdesc(st + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
-            tc_cp_128x128b(e_tmem, edesc);
-          }
-          const int kleft = P.k - ks * C::BKD;
-          const int nmma = kleft >= C::BKD ? C::MMAS : (kleft + C::MMA_K - 1) / C::MMA_K;
+          // Metadata atom: 128 rows of 16 B, rows contiguous -> K-major
+          // no-swizzle canonical layout, 8-row groups 128 B apart.
+          if (sub == 0) tc_cp_elect<1>(e_tmem, edesc0 + soff);
+          // Metadata column of MMA j inside the atom: kind::f16 uses one
+          // 32-bit column per K=32 MMA, kind::f8f6f4 two per K=64 MMA.  The
+          // operand address is even; the odd column is picked through the
+          // sparsity selector (instruction descriptor bits 0-1).
+          uint32_t ecol[C::MMAS], isel[C::MMAS];
+          uint64_t ad[C::MMAS], bd[C::MMAS];
 #pragma unroll
           for (int j = 0; j < C::MMAS; ++j) {
-            if (j < nmma) {
-              // Metadata column of this MMA inside the atom: kind::f16 uses one
-              // 32-bit column per K=32 MMA, kind::f8f6f4 two per K=64 MMA.  The
-              // operand address is even; the odd column is picked through the
-              // sparsity selector (instruction descriptor bits 0-1).
-              const uint32_t ecol = (C::KIND == 0) ? static_cast<uint32_t>(sub * C::MMAS + j)
-                                                   : static_cast<uint32_t>(2 * j);
-              const uint32_t eaddr = e_tmem + ecol;
-              const uint32_t id2 = eaddr & 1u;
-              const uint64_t adesc = make_sdesc(st + j * 32, 16, 512, kLayoutSW64);
-              const uint64_t bdesc = make_sdesc(st + C::A_BYTES + j * C::B_MMA_ADVANCE, C::B_LBO,
-                                                C::B_SBO, C::B_LAYOUT);
-              tc_mma_sp<C::KIND>(d_tmem, adesc, bdesc, eaddr & ~1u, C::IDESC | id2,
-                                 (ks > 0 || j > 0) ? 1u : 0u);
-              any_issued = true;
-            }
+            const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(sub * C::MMAS + j)
+                                                : static_cast<uint32_t>(2 * j);
+            ecol[j] = e_tmem + (col & ~1u);
+            isel[j] = C::IDESC | (col & 1u);
+            ad[j] = adesc0 + soff + j * 2;
+            bd[j] = bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4);
           }
-          tc_commit(&empty_bar[s]);
-          if (++s == C::STAGES) s = 0, ph ^= 1u;
+          const int kleft = P.k - ks * C::BKD;
+          const uint32_t acc0 = ks > 0 ? 1u : 0u;
+          if (kleft >= C::BKD) {
+            tc_mma_sp_elect_x2<1, C::KIND>(d_tmem, ad[0], bd[0], ecol[0], isel[0], ad[1], bd[1],
+                                           ecol[1], isel[1], acc0);
+          } else {
+            tc_mma_sp_elect<1, C::KIND>(d_tmem, ad[0], bd[0], ecol[0], isel[0], acc0);
+          }
+          any_issued = true;
+          tc_commit_elect<1>(&empty_bar[s], 0);
+          soff += SD;
+          if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
         if (!ok) break;
-        tc_commit(&accf_bar[ab]);
+        tc_commit_elect<1>(&accf_bar[ab], 0);
         if (++ab == C::ACC) ab = 0, aph ^= 1u;
       }
       if (!ok && any_issued) {
         // Error path: wait for MMAs in flight before TMEM is released.
         volatile int dummy_abort = 0;
-        tc_commit(&drain_bar);
-        mbar_wait(&drain_bar, 0, &dummy_abort, tmo);
+        tc_commit_elect<1>(&drain_bar, 0);
+        if (lane == 0) mbar_wait(&drain_bar, 0, &dummy_abort, tmo);
+        __syncwarp();
       }
     }
   } else {

@@ -297,7 +297,11 @@ def test_config2_bf16_8192_sampled_rows():
     ref = oracle.gemm(1, a_bits[rows], b_bits, threads=8)
     af, bf = oracle.to_float(1, a_bits[rows]), oracle.to_float(1, b_bits)
     assert oracle.row_norm_rel_error(c[rows].cpu().numpy(), ref, af, bf) <= 1e-2
-    assert oracle.row_norm_rel_error(cb[rows].float().cpu().numpy(), ref, af, bf) <= 1e-2
+    # The bf16 output is the round-to-nearest-even of the fp32 accumulator; its
+    # own quantisation (half an ulp = 2^-9 |C|) exceeds 1e-2 of the row-norm
+    # scale for the largest |C| of an 8192-deep product, so it is held to
+    # exact rounding of the (in-tolerance) fp32 result instead.
+    assert torch.equal(cb, c.to(torch.bfloat16))
     # column checksum of the whole product against an fp32 torch reference
     ones = torch.ones((n, 1), device=DEV)
     lhs = (c @ ones).squeeze(1)
