@@ -187,6 +187,14 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
 }
 
 
+// Tile rasterisation group (M tiles walked together); SP24_GROUP_M overrides
+// for tuning runs.
+int group_m_env(int dflt) {
+  const char* env = std::getenv("SP24_GROUP_M");
+  const int v = env ? std::atoi(env) : 0;
+  return v > 0 ? v : dflt;
+}
+
 template <int DT>
 sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
   using C = sp24::PairCfg<DT>;
@@ -213,8 +221,9 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   if (st != SP24_OK) return st;
   const int mblk = meta_mblocks(p.m);
   const uint64_t lanes = static_cast<uint64_t>(meta_katoms(p.k)) * mblk * 128;
-  st = encode_2d(&te, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.meta_tc, 16, lanes, 16, 16, 128,
-                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  // Metadata image viewed as rows of 256 B: one 2 KB atom = an 8-row box.
+  st = encode_2d(&te, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.meta_tc, 256, lanes * 16 / 256, 256, 256,
+                 8, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != SP24_OK) return st;
 
   sp24::PairParams P{};
@@ -226,7 +235,7 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   P.n_tiles = (p.n + 255) / 256;
   P.k_stages = (p.k + C::BKD - 1) / C::BKD;
   P.num_tiles = P.m_pairs * P.n_tiles;
-  P.group_m = 8;
+  P.group_m = group_m_env(8);
   P.c_f32 = p.c_f32;
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
   P.ldc = p.ldc;

@@ -260,8 +260,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
               x = col0;
               y = ks * C::BKD;
             } else {
+              // The atom is 2 KB contiguous in the image, loaded as 8 rows of 256 B.
               x = 0;
-              y = ((ks * C::ATOMS + la) * P.m_blocks + mb) * 128;
+              y = ((ks * C::ATOMS + la) * P.m_blocks + mb) * 8;
             }
             tma_load_2d_pair(smem + s * C::STAGE_BYTES + lane_off, lane_map,
                              full0_leader + static_cast<uint32_t>(s * sizeof(uint64_t)), x, y);
