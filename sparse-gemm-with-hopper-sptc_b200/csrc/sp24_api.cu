@@ -195,10 +195,10 @@ int group_m_env(int dflt) {
   return v > 0 ? v : dflt;
 }
 
-template <int DT>
+template <int DT, int FINE>
 sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
-  using C = sp24::PairCfg<DT>;
-  auto kern = sp24::sp24_gemm2sm_kernel<DT>;
+  using C = sp24::PairCfg<DT, FINE>;
+  auto kern = sp24::sp24_gemm2sm_kernel<DT, FINE>;
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   SP24_CUDA_TRY(cudaGetDevice(&dev));
@@ -213,7 +213,7 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   sp24_status st =
       encode_2d(&ta, tdt, p.a_c, static_cast<uint64_t>(p.k / 2), static_cast<uint64_t>(p.m),
                 static_cast<uint64_t>(p.lda_c) * C::ESZ, C::A_COLS, sp24::kBlockM,
-                CU_TENSOR_MAP_SWIZZLE_128B);
+                C::A_ROW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   if (st != SP24_OK) return st;
   st = encode_2d(&tb, tdt, p.b, static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.k),
                  static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::BKD,
@@ -255,6 +255,14 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   kern<<<2 * pairs, sp24::kPairThreads, C::SMEM_BYTES, stream>>>(ta, tb, te, P);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
+}
+
+// Stage granularity of the CTA-pair kernel (PairCfg FINE); SP24_PAIR_FINE=0|1
+// overrides for tuning runs.
+bool pair_fine_stages() {
+  const char* env = std::getenv("SP24_PAIR_FINE");
+  if (env != nullptr) return std::atoi(env) != 0;
+  return false;
 }
 
 // Kernel choice: the CTA-pair kernel for problems with at least one full
@@ -399,9 +407,10 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   }
 
   if (use_pair_kernel(d->m, d->n, d->tile_n)) {
-    LaunchFn pf = d->dtype == SP24_F16    ? launch_gemm2sm<0>
-                  : d->dtype == SP24_BF16 ? launch_gemm2sm<1>
-                                          : launch_gemm2sm<2>;
+    const bool fine = pair_fine_stages();
+    LaunchFn pf = d->dtype == SP24_F16    ? (fine ? launch_gemm2sm<0, 1> : launch_gemm2sm<0, 0>)
+                  : d->dtype == SP24_BF16 ? (fine ? launch_gemm2sm<1, 1> : launch_gemm2sm<1, 0>)
+                                          : (fine ? launch_gemm2sm<2, 1> : launch_gemm2sm<2, 0>);
     return pf(p, *di, stream);
   }
   const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);

@@ -10,11 +10,12 @@
 // bound by bytes in flight per SM; this one carries 1.6x the FLOPs per staged
 // byte.  No TMA multicast is used: each CTA loads its own tiles.
 //
-// Roles per CTA (10 warps):
-//   warp 0      TMA producer (both CTAs): A_c rows / B half-columns / the
-//               metadata atom of its own 128 rows; completion bytes of both
-//               CTAs are counted on the leader's (rank 0) full barrier, which
-//               only the leader arms.
+// Roles per CTA (11 warps):
+//   warps 0,10  TMA producers (both CTAs): warp 0 the A_c rows and the
+//               metadata atom of the CTA's own 128 rows, warp 10 its half of
+//               the B columns; completion bytes of both CTAs are counted on
+//               the leader's (rank 0) full barrier, which only the leader's
+//               two producer warps arm.
 //   warp 1      TMEM owner (alloc/dealloc with cta_group::2 in both CTAs);
 //               in the leader one lane issues tcgen05.cp (metadata of both
 //               CTAs into their own TMEM) and the pair MMAs, and commits with
@@ -37,8 +38,9 @@
 
 namespace sp24 {
 
-constexpr int kPairThreads = 320;
+constexpr int kPairThreads = 352;   // 11 warps
 constexpr int kPairEpiWarps = 8;
+constexpr int kPairBWarp = 10;      // second producer warp (B tiles)
 
 struct PairParams {
   int m, n, k;
@@ -57,38 +59,47 @@ struct PairParams {
   int stall_producer;
 };
 
-template <int DT>
+// FINE selects the stage granularity: 0 = 128 dense K per stage for 16-bit
+// types (256 for e4m3), four MMAs per stage; 1 = half of that, two MMAs per
+// stage and twice as many stages.  A ring slot is freed only when its MMAs
+// complete, so the MMAs queued in the tensor pipe hold part of the ring; finer
+// stages leave more of the same shared memory loading.
+template <int DT, int FINE>
 struct PairCfg {
   static constexpr int ESZ = (DT == 2) ? 1 : 2;
   static constexpr int KIND = (DT == 2) ? 1 : 0;
-  static constexpr int BKD = (DT == 2) ? 256 : 128;     // dense K per stage
-  static constexpr int MMA_K = (DT == 2) ? 64 : 32;     // dense K per MMA
-  static constexpr int MMAS = BKD / MMA_K;              // 4 MMAs per stage
-  static constexpr int ATOMS = BKD / 128;               // metadata atoms per stage
-  static constexpr int A_COLS = 128 / ESZ;              // compressed values per stage row
-  static constexpr int A_BYTES = kBlockM * 128;         // SW128 K-major
-  static constexpr int BN = 256;                        // pair tile width
-  static constexpr int BN_CTA = 128;                    // B columns staged per CTA
+  static constexpr int BKD = ((DT == 2) ? 256 : 128) >> FINE;   // dense K per stage
+  static constexpr int MMA_K = (DT == 2) ? 64 : 32;             // dense K per MMA
+  static constexpr int MMAS = BKD / MMA_K;                      // MMAs per stage
+  static constexpr int E_PER = BKD >= 128 ? BKD / 128 : 1;      // atoms loaded with a stage
+  static constexpr int SPA = BKD >= 128 ? 1 : 128 / BKD;        // stages sharing one atom
+  static constexpr int A_ROW = BKD / 2 * ESZ;                   // bytes of a compressed A row
+  static constexpr int A_COLS = A_ROW / ESZ;
+  static constexpr int A_BYTES = kBlockM * A_ROW;
+  static constexpr uint32_t A_LAYOUT = A_ROW == 128 ? kLayoutSW128 : kLayoutSW64;
+  static constexpr uint32_t A_SBO = 8 * A_ROW;                  // 8-row group stride
+  static constexpr int BN = 256;                                // pair tile width
+  static constexpr int BN_CTA = 128;                            // B columns staged per CTA
   static constexpr int B_BOXN = 128 / ESZ;
   static constexpr int B_BOXES = BN_CTA / B_BOXN;
   static constexpr int B_BOX_BYTES = 128 * BKD;
   static constexpr int B_BYTES = B_BOX_BYTES * B_BOXES;
-  static constexpr uint32_t B_LBO = B_BOX_BYTES;        // MN-major SW128: chunk stride
-  static constexpr uint32_t B_SBO = 1024;               // 8-row K group stride
+  static constexpr uint32_t B_LBO = B_BOX_BYTES;                // MN-major SW128: chunk stride
+  static constexpr uint32_t B_SBO = 1024;                       // 8-row K group stride
   static constexpr int B_MMA_ADVANCE = MMA_K * 128;
-  static constexpr int E_BYTES = ATOMS * kAtomBytes;
+  static constexpr int E_BYTES = E_PER * kAtomBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
   static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-  static constexpr int LOADS = 1 + B_BOXES + ATOMS;     // TMA boxes per stage per CTA
-  static constexpr int E_COL = 256;                     // two buffers of ATOMS*4 columns
+  static constexpr int LOADS = 1 + B_BOXES + E_PER;             // TMA boxes per stage per CTA
+  static constexpr int E_COL = 256;                             // two buffers of E_PER*4 columns
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
   static constexpr uint32_t IDESC = make_idesc_sparse(FMT, 256, 256, true);
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
-  static_assert(MMAS == 4, "full stages are issued as one block of four MMAs");
+  static_assert(MMAS == 4 || MMAS == 2, "full stages are issued as one block of MMAs");
   static_assert(LOADS <= 32, "one lane per TMA box");
 };
 
@@ -162,13 +173,13 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
   }
 }
 
-template <int DT>
+template <int DT, int FINE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     sp24_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmE, const PairParams P) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using C = PairCfg<DT>;
+  using C = PairCfg<DT, FINE>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -190,13 +201,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   if (threadIdx.x == 0) {
     abort_sh = 0;
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      mbar_init(&full_bar[s], C::SPA == 1 ? 1 : 2);  // fine stages: one arming per producer warp
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&accf_bar, 1);
     mbar_init(&acce_bar, 2 * kPairEpiWarps);
     mbar_init(&drain_bar, 1);
     fence_barrier_init();
+    // Coarse stages all carry the same bytes, so the leader arms every full
+    // barrier for its first use here and the MMA warp re-arms a slot for its
+    // next use as soon as it has seen the slot's data arrive: the producers'
+    // per-stage work shrinks to one slot wait and one TMA issue.
+    if constexpr (C::SPA == 1) {
+      if (leader)
+        for (int s = 0; s < C::STAGES; ++s) mbar_arrive_expect_tx(&full_bar[s], 2u * C::STAGE_BYTES);
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -213,31 +232,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t tmem_base = tmem_base_sh;
   const uint64_t tmo = P.timeout_ns;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    // The whole warp runs the loop; lane i issues the i-th TMA box of a stage
-    // (A_c, B chunks, metadata atoms), so one warp instruction covers a stage.
+  if (warp == 0 || warp == kPairBWarp) {
+    // ------------------------------------------------------------ producers
+    // Two warps load each stage: warp 0 the A_c box (lane 0) and the metadata
+    // atoms (lanes 1..E_PER), warp 10 the B boxes (one per lane).  Splitting
+    // the stage halves the serial chain of shared-memory operations (slot
+    // wait, expect_tx, TMA issue) each warp runs per stage; under full
+    // tensor-core load every one of those operations queues behind the
+    // MMA's operand reads.  Per lane, the box coordinates advance by a
+    // constant step per stage.  Completion bytes of both CTAs land on the
+    // leader's full barrier, which each leader warp arms with its share.
     if (!P.stall_producer) {
+      const bool is_b = warp == kPairBWarp;
       const uint32_t full0_leader = mapa_shared(smem_u32(&full_bar[0]), 0);
-      const CUtensorMap* lane_map =
-          lane == 0 ? &tmA : (lane <= C::B_BOXES ? &tmB : &tmE);
-      const int lb = lane - 1;                    // B chunk of lanes 1..B_BOXES
-      const int la = lane - 1 - C::B_BOXES;       // metadata atom of the last lanes
+      const CUtensorMap* lane_map = is_b ? &tmB : (lane == 0 ? &tmA : &tmE);
       const uint32_t lane_off =
-          lane == 0 ? 0u
-                    : (lane <= C::B_BOXES ? static_cast<uint32_t>(C::A_BYTES + lb * C::B_BOX_BYTES)
-                                          : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES +
-                                                                  la * kAtomBytes));
+          is_b ? static_cast<uint32_t>(C::A_BYTES + lane * C::B_BOX_BYTES)
+               : (lane == 0 ? 0u
+                            : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES +
+                                                    (lane - 1) * kAtomBytes));
+      const int lanes_e = is_b ? C::B_BOXES : 1 + C::E_PER;  // stages that carry metadata
+      const int lanes_n = is_b ? C::B_BOXES : 1;             // stages that do not
+      const uint32_t tx_e = 2u * (is_b ? C::B_BYTES : C::A_BYTES + C::E_BYTES);
+      const uint32_t tx_n = 2u * (is_b ? C::B_BYTES : C::A_BYTES);
+      const int dx = (!is_b && lane == 0) ? C::A_COLS : 0;
+      const int dy = is_b ? C::BKD : (lane == 0 ? 0 : C::E_PER * P.m_blocks * 8 / C::SPA);
       int s = 0;
       uint32_t ph = 0;
+      uint32_t soff = 0;
       bool ok = true;
       uint32_t armed_mask = 0, armed_ph = 0;
       for (int t = pair; t < P.num_tiles && ok; t += npairs) {
         int mp, nb;
         pair_tile_coords(P, t, mp, nb);
         const int row0 = mp * 256 + static_cast<int>(rank) * 128;
-        const int col0 = nb * 256 + static_cast<int>(rank) * 128 + lb * C::B_BOXN;
         const int mb = mp * 2 + static_cast<int>(rank);
+        int x = is_b ? nb * 256 + static_cast<int>(rank) * 128 + lane * C::B_BOXN : 0;
+        int y = is_b ? 0 : (lane == 0 ? row0 : ((lane - 1) * P.m_blocks + mb) * 8);
         for (int ks = 0; ks < P.k_stages; ++ks) {
           int good = 1;
           if (lane == 0) good = mbar_wait_fast(&empty_bar[s], ph ^ 1u, &abort_sh, tmo) ? 1 : 0;
@@ -245,29 +276,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ok = false;
             break;
           }
+          const bool with_e = (C::SPA == 1) || (ks % C::SPA) == 0;
+          if constexpr (C::SPA != 1) {
+            if (leader && lane == 0) mbar_arrive_expect_tx(&full_bar[s], with_e ? tx_e : tx_n);
+            __syncwarp();
+          }
           if (leader && lane == 0) {
-            mbar_arrive_expect_tx(&full_bar[s], 2u * C::STAGE_BYTES);
             armed_mask |= 1u << s;
             armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
           }
-          __syncwarp();
-          if (lane < C::LOADS) {
-            int x, y;
-            if (lane == 0) {
-              x = ks * C::A_COLS;
-              y = row0;
-            } else if (lane <= C::B_BOXES) {
-              x = col0;
-              y = ks * C::BKD;
-            } else {
-              // The atom is 2 KB contiguous in the image, loaded as 8 rows of 256 B.
-              x = 0;
-              y = ((ks * C::ATOMS + la) * P.m_blocks + mb) * 8;
-            }
-            tma_load_2d_pair(smem + s * C::STAGE_BYTES + lane_off, lane_map,
+          if (lane < (with_e ? lanes_e : lanes_n))
+            tma_load_2d_pair(smem + soff + lane_off, lane_map,
                              full0_leader + static_cast<uint32_t>(s * sizeof(uint64_t)), x, y);
-          }
-          if (++s == C::STAGES) s = 0, ph ^= 1u;
+          x += dx;
+          y += dy;
+          soff += C::STAGE_BYTES;
+          if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
       }
       if (!ok && leader && lane == 0) {
@@ -283,25 +307,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // Descriptors are formed once; per stage only the start-address field
     // moves (stage offset >> 4 added to the 64-bit descriptor), per MMA by a
     // compile-time step.  Metadata: atom a of a stage lives in TMEM columns
-    // E_COL + ebuf*ATOMS*4 + a*4; kind::f16 MMAs use one column each (odd
+    // E_COL + ebuf + a*4 (ebuf alternates between two buffers of E_PER*4
+    // columns per atom group); kind::f16 MMAs use one column each (odd
     // columns through the sparsity selector), kind::f8f6f4 MMAs two.
     if (leader) {
       const uint32_t smem_base = smem_u32(smem);
-      const uint64_t adesc0 = make_sdesc(smem_base, 16, 1024, kLayoutSW128);
+      const uint64_t adesc0 = make_sdesc(smem_base, 16, C::A_SBO, C::A_LAYOUT);
       const uint64_t bdesc0 = make_sdesc(smem_base + C::A_BYTES, C::B_LBO, C::B_SBO, kLayoutSW128);
       const uint64_t edesc0 =
           make_sdesc(smem_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
       constexpr uint32_t SD = C::STAGE_BYTES >> 4;
       constexpr int kPerAtom = 128 / C::MMA_K;
-      // Per-MMA constants: metadata column offset and sparsity selector.
-      uint32_t ecol[C::MMAS], isel[C::MMAS];
+      // Per-MMA constants, per position `sub` of the stage inside its atom
+      // group: metadata column offset and sparsity selector.
+      uint32_t ecol[C::SPA][C::MMAS], isel[C::SPA][C::MMAS];
 #pragma unroll
-      for (int j = 0; j < C::MMAS; ++j) {
-        const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(j % kPerAtom)
-                                            : static_cast<uint32_t>(2 * (j % kPerAtom));
-        ecol[j] = 4u * static_cast<uint32_t>(j / kPerAtom) + (col & ~1u);
-        isel[j] = C::IDESC | (col & 1u);
-      }
+      for (int sb = 0; sb < C::SPA; ++sb)
+#pragma unroll
+        for (int j = 0; j < C::MMAS; ++j) {
+          const int koff = sb * C::BKD + j * C::MMA_K;          // dense K inside the group
+          const int kin = (koff % 128) / C::MMA_K;              // MMA index inside its atom
+          const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(kin)
+                                              : static_cast<uint32_t>(2 * kin);
+          ecol[sb][j] = 4u * static_cast<uint32_t>(koff / 128) + (col & ~1u);
+          isel[sb][j] = C::IDESC | (col & 1u);
+        }
+      (void)kPerAtom;
       int s = 0;
       uint32_t ph = 0, soff = 0, aph = 0, ebuf = 0;
       bool ok = true, any = false;
@@ -316,33 +347,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ok = false;
             break;
           }
+          if constexpr (C::SPA == 1) {
+            if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], 2u * C::STAGE_BYTES);
+          }
           tc_fence_after();
+          const int sub = ks % C::SPA;
+          if (sub == 0) ebuf ^= static_cast<uint32_t>(C::E_PER * 4);
           const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
+          if (sub == 0) {
 #pragma unroll
-          for (int a = 0; a < C::ATOMS; ++a)
-            tc_cp_elect<2>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
+            for (int a = 0; a < C::E_PER; ++a)
+              tc_cp_elect<2>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
+          }
           const int kleft = P.k - ks * C::BKD;
           const uint32_t acc0 = ks > 0 ? 1u : 0u;
           uint64_t ad[C::MMAS], bd[C::MMAS];
-          uint32_t ed[C::MMAS];
+          uint32_t ed[C::MMAS], id[C::MMAS];
 #pragma unroll
           for (int j = 0; j < C::MMAS; ++j) {
             ad[j] = adesc0 + soff + j * 2;
             bd[j] = bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4);
-            ed[j] = e_tmem + ecol[j];
+            ed[j] = e_tmem + (C::SPA == 1 ? ecol[0][j] : ecol[sub & (C::SPA - 1)][j]);
+            id[j] = C::SPA == 1 ? isel[0][j] : isel[sub & (C::SPA - 1)][j];
           }
           if (kleft >= C::BKD) {
-            tc_mma_sp_elect_x4<2, C::KIND>(tmem_base, ad, bd, ed, isel, acc0);
+            if constexpr (C::MMAS == 4) {
+              tc_mma_sp_elect_x4<2, C::KIND>(tmem_base, ad, bd, ed, id, acc0);
+            } else {
+              tc_mma_sp_elect_x2<2, C::KIND>(tmem_base, ad[0], bd[0], ed[0], id[0], ad[1], bd[1],
+                                             ed[1], id[1], acc0);
+            }
           } else {
 #pragma unroll
             for (int j = 0; j < C::MMAS; ++j)
               if (j * C::MMA_K < kleft)
-                tc_mma_sp_elect<2, C::KIND>(tmem_base, ad[j], bd[j], ed[j], isel[j],
+                tc_mma_sp_elect<2, C::KIND>(tmem_base, ad[j], bd[j], ed[j], id[j],
                                             j > 0 ? 1u : acc0);
           }
           any = true;
           tc_commit_elect<2>(&empty_bar[s], static_cast<uint16_t>(3));
-          ebuf ^= static_cast<uint32_t>(C::ATOMS * 4);
           soff += SD;
           if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
@@ -367,7 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       int mp, nb;
       pair_tile_coords(P, t, mp, nb);
       bool ok = true;
-      if (lane == 0) ok = mbar_wait(&accf_bar, aph, &abort_sh, tmo);
+      if (lane == 0) ok = mbar_wait_sleepy(&accf_bar, aph, &abort_sh, tmo);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       tc_fence_after();

@@ -104,6 +104,29 @@ SP24_DEV bool mbar_wait_fast(uint64_t* bar, uint32_t parity, volatile int* abort
   return mbar_wait_slow<kCluster>(bar, parity, abort, timeout_ns);
 }
 
+// Bounded wait for long waits on a busy SM (e.g. epilogue warps waiting for
+// a whole tile): after a few polls it sleeps between polls, so idle waiters
+// do not compete with the producers and the MMA issuer for issue slots and
+// shared-memory bandwidth.
+SP24_DEV bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, volatile int* abort,
+                               uint64_t timeout_ns) {
+  if (mbar_try_wait<false>(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait<false>(bar, parity)) return true;
+    ++it;
+    if (it > 8) __nanosleep(256);
+    if ((it & 15u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > timeout_ns || it > (1u << 26)) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 template <bool kCluster = false>
 SP24_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t timeout_ns) {
   if (mbar_try_wait<kCluster>(bar, parity)) return true;
