@@ -50,7 +50,9 @@ typedef enum sp24_status {
   SP24_ERR_TIMEOUT = 6,    /* a bounded device-side wait gave up; the kernel returned early */
   SP24_ERR_NCCL = 7,       /* collective failure (multi-GPU all-gather) */
   SP24_ERR_ARG = 8,        /* NULL pointer / bad enum */
-  SP24_ERR_WORKSPACE = 9   /* workspace missing or too small */
+  SP24_ERR_WORKSPACE = 9,  /* workspace missing or too small */
+  SP24_ERR_SCRATCH_LIMIT = 10 /* sp24_gemm_noalloc: the problem needs more scratch than the
+                                 library's fixed device buffer (SP24_NOALLOC_SCRATCH_BYTES) */
 } sp24_status;
 
 typedef enum sp24_dtype {
@@ -142,6 +144,29 @@ sp24_status sp24_last_kernel_status(sp24_stream_t stream);
    SP24_OK if no wait ran out. */
 sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long timeout_ns,
                                   sp24_stream_t stream);
+
+/* Allocation-free GEMM (no counterpart in the reference).
+   Same contract and results as sp24_gemm, for callers that must not allocate
+   device memory per call: code running inside a stream-capture region or a
+   real-time serving loop that forbids cudaMalloc/cudaFree after start-up, and
+   plugin hosts that hand the library only its inputs and outputs.  Instead of
+   d->workspace (ignored here) it stages its scratch (the tcgen05 image of
+   reference-layout metadata and, when B's row pitch breaks the 16-byte TMA
+   rule, a padded copy of B) in one fixed buffer of SP24_NOALLOC_SCRATCH_BYTES
+   bytes that lives in the library's device image: every GPU that loads the
+   library holds it until the process exits.
+   - Problems whose scratch need (sp24_gemm_workspace_bytes) exceeds the
+     buffer are rejected with SP24_ERR_SCRATCH_LIMIT; nothing is launched.
+   - The buffer is shared by every call on a device and keeps the previous
+     call's contents; calls that can overlap on the GPU (different streams
+     without ordering) race on it.  Serialize them, or use sp24_gemm with
+     caller-owned workspaces.
+   - The first call on a device looks the buffer's device address up (once,
+     with that device current); make that first call before any stream
+     capture begins.
+   It calls no cudaMalloc, cudaFree or other allocating routine. */
+#define SP24_NOALLOC_SCRATCH_BYTES (16u << 20)
+sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream);
 
 /* FP8 helpers for the e4m3 path.
    sp24_amax_f32: amax_dev[0] = max |x| over count floats (device).

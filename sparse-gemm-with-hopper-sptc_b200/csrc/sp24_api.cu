@@ -27,6 +27,11 @@ constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per boun
 // Library-owned per-device status word used when the caller passes none.
 __device__ int g_sp24_status_word;
 
+// Fixed scratch of sp24_gemm_noalloc.  In host code this name is only a
+// stand-in for the symbol: its device address comes from cudaGetSymbolAddress
+// (noalloc_scratch below), looked up once per device with that device current.
+static __device__ __align__(256) uint8_t g_sp24_noalloc_scratch[SP24_NOALLOC_SCRATCH_BYTES];
+
 #define SP24_CUDA_TRY(expr)                  \
   do {                                       \
     cudaError_t e__ = (expr);                \
@@ -420,6 +425,28 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   return fn(p, *di, stream);
 }
 
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices];
+
+// Device address of the no-alloc scratch for the current device.
+sp24_status noalloc_scratch(void** out) {
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return SP24_ERR_ARG;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_sp24_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
+      return SP24_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SP24_OK;
+}
+
 unsigned int grid_for(long long work, int block) {
   long long g = (work + block - 1) / block;
   if (g < 1) g = 1;
@@ -444,6 +471,8 @@ const char* sp24_status_string(sp24_status s) {
     case SP24_ERR_NCCL: return "NCCL error";
     case SP24_ERR_ARG: return "invalid argument";
     case SP24_ERR_WORKSPACE: return "workspace missing or too small";
+    case SP24_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the no-alloc buffer (SP24_NOALLOC_SCRATCH_BYTES)";
   }
   return "unknown status";
 }
@@ -469,6 +498,21 @@ size_t sp24_gemm_workspace_bytes(const sp24_gemm_desc* d) {
 
 sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream) {
   return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0);
+}
+
+// Allocation-free sp24_gemm: the scratch sp24_gemm would take from
+// d->workspace comes from the fixed device buffer g_sp24_noalloc_scratch.
+sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream) {
+  sp24_status st = validate(d);
+  if (st != SP24_OK) return st;
+  if (plan_workspace(d).total > SP24_NOALLOC_SCRATCH_BYTES) return SP24_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st != SP24_OK) return st;
+  sp24_gemm_desc local = *d;
+  local.workspace = scratch;
+  local.workspace_bytes = SP24_NOALLOC_SCRATCH_BYTES;
+  return gemm_impl(&local, as_stream(stream), kDefaultTimeoutNs, 0);
 }
 
 // Self-test of the bounded-wait path: runs the GEMM with a producer that

@@ -26,7 +26,7 @@ META_REF, META_TC = 0, 1
 STATUS = {
     0: "SP24_OK", 1: "SP24_ERR_SHAPE", 2: "SP24_ERR_ALIGN", 3: "SP24_ERR_NOT_2OF4",
     4: "SP24_ERR_ARCH", 5: "SP24_ERR_CUDA", 6: "SP24_ERR_TIMEOUT", 7: "SP24_ERR_NCCL",
-    8: "SP24_ERR_ARG", 9: "SP24_ERR_WORKSPACE",
+    8: "SP24_ERR_ARG", 9: "SP24_ERR_WORKSPACE", 10: "SP24_ERR_SCRATCH_LIMIT",
 }
 
 # Every symbol include/sp24.h declares.
@@ -35,6 +35,7 @@ EXPORTS = [
     "sp24_gemm_workspace_bytes", "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta",
     "sp24_gemm", "sp24_last_kernel_status", "sp24_selftest_timeout", "sp24_amax_f32",
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
+    "sp24_gemm_noalloc",
 ]
 
 
@@ -77,6 +78,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_gemm_workspace_bytes.restype = c_size_t
     lib.sp24_gemm_workspace_bytes.argtypes = [POINTER(GemmDesc)]
     lib.sp24_gemm.argtypes = [POINTER(GemmDesc), c_void_p]
+    lib.sp24_gemm_noalloc.argtypes = [POINTER(GemmDesc), c_void_p]
     lib.sp24_selftest_timeout.argtypes = [POINTER(GemmDesc), c_ulonglong, c_void_p]
     lib.sp24_last_kernel_status.argtypes = [c_void_p]
     lib.sp24_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
@@ -92,7 +94,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                        POINTER(c_int)]
     lib.sp24_unshard_columns_f32.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                              c_void_p]
-    for name in ("sp24_gemm", "sp24_selftest_timeout", "sp24_last_kernel_status",
+    for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_selftest_timeout", "sp24_last_kernel_status",
                  "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_amax_f32",
                  "sp24_quantize_e4m3", "sp24_unshard_columns_f32", "sp24_check_device"):
         getattr(lib, name).restype = c_int
