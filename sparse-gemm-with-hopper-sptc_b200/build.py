@@ -29,7 +29,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall"]
 
 LIB_SOURCES = ["sp24_api.cu"]
-LIB_DEPS = ["sp24_api.cu", "sp24_gemm_kernel.cuh", "sp24_gemm2sm_kernel.cuh", "sp24_prep.cuh",
+LIB_DEPS = ["sp24_api.cu", "sp24_gemm_kernel.cuh", "sp24_gemm2sm_kernel.cuh",
+            "sp24_gemm_splitk_kernel.cuh", "sp24_prep.cuh",
             "sp24_ptx.cuh"]
 
 

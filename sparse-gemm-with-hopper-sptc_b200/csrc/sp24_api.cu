@@ -17,6 +17,7 @@
 #include "../../include/sp24.h"
 #include "sp24_gemm2sm_kernel.cuh"
 #include "sp24_gemm_kernel.cuh"
+#include "sp24_gemm_splitk_kernel.cuh"
 #include "sp24_prep.cuh"
 
 namespace {
@@ -262,6 +263,124 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   return SP24_OK;
 }
 
+// Largest cluster of split-K CTAs the device keeps resident `tiles` times
+// over (cached per device and split factor).
+std::mutex g_occ_mu;
+int g_occ[kMaxDevices][sp24::kMaxSplits + 1];
+
+template <typename Kern>
+int max_active_clusters(Kern kern, int smem, int splits) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  int& slot = g_occ[dev][splits];
+  if (slot == 0) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(splits));
+    cfg.blockDim = dim3(sp24::kThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    slot = n > 0 ? n : -1;
+  }
+  return slot;
+}
+
+// K-split factor of the narrow-N kernel.  When the 128-row tiles already
+// cover three quarters of the SMs the tiles run unsplit; otherwise K is cut
+// into as many slices as there are SMs per tile (at most 8, the portable
+// cluster size, and at least two stages per slice), and the factor is
+// lowered until all clusters are resident at once.  SP24_SPLITS overrides
+// (tests and tuning runs; still clamped to those limits).
+template <typename Kern>
+int choose_splits(Kern kern, int smem, int tiles, int stages, int sm_count) {
+  const char* env = std::getenv("SP24_SPLITS");
+  const int forced = env ? std::atoi(env) : 0;
+  int s = forced > 0 ? forced : (tiles * 4 >= sm_count * 3 ? 1 : sm_count / tiles);
+  s = std::min(s, sp24::kMaxSplits);
+  s = std::min(s, std::max(1, forced > 0 ? stages : stages / 2));
+  s = std::max(s, 1);
+  if (forced <= 0)
+    while (s > 1 && max_active_clusters(kern, smem, s) < tiles) --s;
+  return s;
+}
+
+template <int DT, int BN, int KB>
+sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
+  using C = sp24::SplitCfg<DT, BN, KB>;
+  auto kern = sp24::sp24_gemm_splitk_kernel<DT, BN, KB>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    SP24_CUDA_TRY(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const CUtensorMapDataType tdt =
+      C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUtensorMap ta, tb;
+  sp24_status st =
+      encode_2d(&ta, tdt, p.a_c, static_cast<uint64_t>(p.k / 2), static_cast<uint64_t>(p.m),
+                static_cast<uint64_t>(p.lda_c) * C::ESZ, C::A_COLS, sp24::kBlockM,
+                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != SP24_OK) return st;
+  st = encode_2d(&tb, tdt, p.b, static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.k),
+                 static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::UK,
+                 swizzle_for_span(C::B_SPAN));
+  if (st != SP24_OK) return st;
+
+  sp24::SplitParams P{};
+  P.m = p.m;
+  P.n = p.n;
+  P.k = p.k;
+  P.m_blocks = (p.m + sp24::kBlockM - 1) / sp24::kBlockM;
+  P.n_tiles = (p.n + BN - 1) / BN;
+  P.stages = (p.k + C::BKD - 1) / C::BKD;
+  P.katoms = meta_katoms(p.k);
+  P.meta_tc = p.meta_tc;
+  P.meta_mblocks = meta_mblocks(p.m);
+  P.c_f32 = p.c_f32;
+  P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
+  P.ldc = p.ldc;
+  P.alpha = p.alpha;
+  P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
+  P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
+  P.status = p.status;
+  P.timeout_ns = p.timeout_ns;
+  P.stall_producer = p.stall_producer;
+  const int tiles = P.m_blocks * P.n_tiles;
+  P.splits = choose_splits(kern, C::SMEM_BYTES, tiles, P.stages, di.sm_count);
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * P.splits));
+  cfg.blockDim = dim3(sp24::kThreads);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(P.splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SP24_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, P));
+  return SP24_OK;
+}
+
 // Stage granularity of the CTA-pair kernel (PairCfg FINE); SP24_PAIR_FINE=0|1
 // overrides for tuning runs.
 bool pair_fine_stages() {
@@ -281,7 +400,40 @@ bool use_pair_kernel(int m, int n, int hint) {
   return m >= 256 && n >= 256;
 }
 
+// Tiles at most 128 wide take the split-K kernel when N itself is narrow or
+// the tile count is modest (up to four waves): there its large stages and
+// K splitting win.  With thousands of narrow tiles the persistent
+// single-CTA kernel, whose grouped tile order shares operands in L2, is
+// faster.  SP24_KERNEL=1sm|splitk overrides.
+bool use_splitk_kernel(int m, int n, int bn, int sm_count) {
+  const char* env = std::getenv("SP24_KERNEL");
+  if (env != nullptr && std::strcmp(env, "1sm") == 0) return false;
+  if (bn > 128) return false;
+  if (env != nullptr && std::strcmp(env, "splitk") == 0) return true;
+  const long long tiles = static_cast<long long>((m + 127) / 128) * ((n + bn - 1) / bn);
+  return n <= 128 || tiles <= 4LL * sm_count;
+}
+
+// Units per split-K stage: two (32 KB of A_c) for tiles up to 32 wide, one
+// above, where B's share of a stage grows.  SP24_SPLITK_KB=1|2 overrides.
+int splitk_units(int bn) {
+  const char* env = std::getenv("SP24_SPLITK_KB");
+  const int v = env ? std::atoi(env) : 0;
+  if (v == 1 || v == 2) return v;
+  return bn <= 32 ? 2 : 1;
+}
+
 using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t);
+
+template <int DT>
+LaunchFn pick_splitk(int bn, int kb) {
+  switch (bn) {
+    case 16: return kb == 2 ? launch_splitk<DT, 16, 2> : launch_splitk<DT, 16, 1>;
+    case 32: return kb == 2 ? launch_splitk<DT, 32, 2> : launch_splitk<DT, 32, 1>;
+    case 64: return kb == 2 ? launch_splitk<DT, 64, 2> : launch_splitk<DT, 64, 1>;
+    default: return kb == 2 ? launch_splitk<DT, 128, 2> : launch_splitk<DT, 128, 1>;
+  }
+}
 
 template <int DT>
 LaunchFn pick_bn(int bn) {
@@ -419,6 +571,13 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     return pf(p, *di, stream);
   }
   const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);
+  if (use_splitk_kernel(d->m, d->n, bn, di->sm_count)) {
+    const int kb = splitk_units(bn);
+    LaunchFn sf = d->dtype == SP24_F16    ? pick_splitk<0>(bn, kb)
+                  : d->dtype == SP24_BF16 ? pick_splitk<1>(bn, kb)
+                                          : pick_splitk<2>(bn, kb);
+    return sf(p, *di, stream);
+  }
   LaunchFn fn = d->dtype == SP24_F16    ? pick_bn<0>(bn)
                 : d->dtype == SP24_BF16 ? pick_bn<1>(bn)
                                         : pick_bn<2>(bn);

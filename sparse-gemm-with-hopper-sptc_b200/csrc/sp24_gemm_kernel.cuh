@@ -116,8 +116,9 @@ SP24_DEV void tile_coords(const GemmParams& P, int t, int& mb, int& nb) {
   nb = r / gm;
 }
 
-template <int N>
-SP24_DEV void store_chunk(const GemmParams& P, uint32_t (&r)[N], int row, int col) {
+// PP: any parameter block with m, n, ldc, alpha, c_f32, c_bf16, vec_f32, vec_bf16.
+template <int N, typename PP>
+SP24_DEV void store_chunk(const PP& P, uint32_t (&r)[N], int row, int col) {
   if (row >= P.m) return;
   const float alpha = P.alpha;
   float v[N];

@@ -1,0 +1,401 @@
+// sp24_gemm_splitk_kernel.cuh — the narrow-N 2:4 sparse GEMM (N <= 128):
+// large K stages, and split-K across a thread-block cluster reduced through
+// distributed shared memory.
+//
+// With few output columns (an MLP layer applied to a handful of tokens) the
+// GEMM is bound by streaming A_c and its metadata from HBM once: per 128-row
+// tile the MMAs are tiny and nearly all time goes to moving bytes.  Two things
+// decide the rate: the bytes each SM keeps in flight and the number of SMs
+// streaming.  This kernel therefore
+//   * stages KB "units" per ring slot, a unit being one 128 x 128 B A_c box
+//     (SWIZZLE_128B; 128 dense K for 16-bit types, 256 for e4m3), the B rows
+//     of the same K range and their metadata atoms, so one slot carries 22-50
+//     KB and the ring keeps ~200 KB per SM in flight;
+//   * arms every full barrier for its first use at start-up and lets the MMA
+//     warp re-arm a slot as soon as it has seen the slot fill, so the
+//     producer warp only waits for a free slot and issues its TMA copies, one
+//     copy per lane;
+//   * splits K over the S CTAs of a cluster (S <= 8) when the 128-row tiles
+//     alone cannot occupy the GPU.  Each CTA accumulates its K range in TMEM,
+//     parks the fp32 partial tile in its own shared memory, and after a
+//     cluster barrier CTA r sums rows [128 r / S, 128 (r+1) / S) of all S
+//     partials over DSMEM in rank order (a fixed order: results do not depend
+//     on timing) and stores them.  No workspace, no atomics, no second launch.
+//
+// Roles (6 warps, as in sp24_gemm_kernel.cuh): warp 0 TMA producer, warp 1
+// TMEM owner and MMA issuer, warps 2..5 epilogue (TMEM lane quarters).
+//
+// Replaces, for narrow N, the reference's wgmma_sp_raw_kernel<Element,BlockN>
+// (wgmma_sp_raw_common.hpp:955-1030), whose BlockN 8..128 variants compute one
+// 64 x BlockN tile per CTA with one 32/64-wide K step per iteration.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "sp24_gemm_kernel.cuh"
+#include "sp24_ptx.cuh"
+
+namespace sp24 {
+
+constexpr int kMaxSplits = 8;
+
+struct SplitParams {
+  int m, n, k;
+  int m_blocks, n_tiles;
+  int splits;         // S: CTAs per cluster, each owning a contiguous range of stages
+  int stages;         // ceil(K / dense K per stage)
+  int katoms;         // metadata atoms along K (ceil(K / 128))
+  const uint8_t* meta_tc;
+  int meta_mblocks;
+  float* c_f32;
+  __nv_bfloat16* c_bf16;
+  long long ldc;
+  float alpha;
+  int vec_f32;
+  int vec_bf16;
+  int* status;
+  unsigned long long timeout_ns;
+  int stall_producer;
+};
+
+template <int DT, int BN, int KB>
+struct SplitCfg {
+  static constexpr int ESZ = (DT == 2) ? 1 : 2;
+  static constexpr int KIND = (DT == 2) ? 1 : 0;
+  static constexpr int UK = (DT == 2) ? 256 : 128;        // dense K per unit
+  static constexpr int MMA_K = (DT == 2) ? 64 : 32;
+  static constexpr int MMAS_U = UK / MMA_K;               // 4
+  static constexpr int E_U = UK / 128;                    // metadata atoms per unit
+  static constexpr int BKD = KB * UK;                     // dense K per stage
+  static constexpr int A_COLS = 128 / ESZ;                // compressed values per A box row
+  static constexpr int A_BOX = kBlockM * 128;             // 16 KB
+  static constexpr int A_BYTES = KB * A_BOX;
+  static constexpr int B_ROW = BN * ESZ;
+  static constexpr int B_SPAN = B_ROW >= 128 ? 128 : B_ROW;
+  static constexpr int B_BOXN = B_SPAN / ESZ;
+  static constexpr int B_BOXES = BN / B_BOXN;             // per unit
+  static constexpr int B_BOX_BYTES = B_SPAN * UK;
+  static constexpr int B_UNIT = B_BOX_BYTES * B_BOXES;
+  static constexpr int B_BYTES = KB * B_UNIT;
+  static constexpr uint32_t B_LAYOUT =
+      B_SPAN == 128 ? kLayoutSW128 : B_SPAN == 64 ? kLayoutSW64 : B_SPAN == 32 ? kLayoutSW32
+                                                                             : kLayoutNone;
+  static constexpr uint32_t B_LBO = B_LAYOUT == kLayoutNone ? 8 * B_SPAN : B_BOX_BYTES;
+  static constexpr uint32_t B_SBO = B_LAYOUT == kLayoutNone ? B_BOX_BYTES : 8 * B_SPAN;
+  static constexpr int B_MMA_ADVANCE = MMA_K * B_SPAN;
+  static constexpr int E_S = KB * E_U;                    // metadata atoms per stage
+  static constexpr int E_BYTES = E_S * kAtomBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
+  static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int LOADS_A = KB;
+  static constexpr int LOADS_B = KB * B_BOXES;
+  static constexpr int LOADS = LOADS_A + LOADS_B + E_S;   // one copy per producer lane
+  static constexpr uint32_t LOAD_LANES = LOADS == 32 ? 0xffffffffu : (1u << LOADS) - 1u;
+  static constexpr int COLS_NEEDED = BN + 2 * E_S * 4;
+  static constexpr uint32_t TMEM_COLS = COLS_NEEDED <= 32    ? 32
+                                        : COLS_NEEDED <= 64  ? 64
+                                        : COLS_NEEDED <= 128 ? 128
+                                        : COLS_NEEDED <= 256 ? 256
+                                                             : 512;
+  static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
+  static constexpr uint32_t IDESC = make_idesc_sparse(FMT, BN, kBlockM, true);
+  static constexpr int CH = BN < 32 ? BN : 32;
+  static constexpr int RS = BN + 4;                       // partial-tile row stride (floats)
+
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 128, "narrow tiles: N % 16 == 0, 16..128");
+  static_assert(BN % B_BOXN == 0, "B tile must be whole TMA boxes");
+  static_assert(STAGES >= 2, "shared memory too small for two stages");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
+  static_assert(LOADS <= 32, "one producer lane per copy");
+  static_assert(kBlockM * RS * 4 <= STAGES * STAGE_BYTES, "partial tile must fit the ring");
+};
+
+// Bytes that land on a slot's full barrier for global stage g: every A and B
+// box counts in full (TMA counts zero-filled out-of-range elements too);
+// metadata atoms past the image are not loaded.
+template <class C>
+SP24_DEV uint32_t split_stage_tx(const SplitParams& P, int g) {
+  const int a0 = g * C::E_S;
+  int atoms = P.katoms - a0;
+  atoms = atoms < 0 ? 0 : (atoms > C::E_S ? C::E_S : atoms);
+  return static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + atoms * kAtomBytes);
+}
+
+template <typename PP>
+SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
+  if (row >= P.m) return;
+  const float alpha = P.alpha;
+  v.x *= alpha;
+  v.y *= alpha;
+  v.z *= alpha;
+  v.w *= alpha;
+  const bool full = col + 4 <= P.n;
+  if (P.c_f32 != nullptr) {
+    float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col;
+    if (full && P.vec_f32) {
+      *reinterpret_cast<float4*>(dst) = v;
+    } else {
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (col + i < P.n) dst[i] = e[i];
+    }
+  }
+  if (P.c_bf16 != nullptr) {
+    __nv_bfloat16* dst = P.c_bf16 + static_cast<long long>(row) * P.ldc + col;
+    if (full && P.vec_bf16) {
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(v.z, v.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&h0);
+      pk.y = *reinterpret_cast<uint32_t*>(&h1);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    } else {
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (col + i < P.n) dst[i] = __float2bfloat16_rn(e[i]);
+    }
+  }
+}
+
+// Grid: (m_blocks * n_tiles * S) CTAs in clusters of S along x; CTA rank r of
+// cluster t computes tile t over stages [stages*r/S, stages*(r+1)/S).
+template <int DT, int BN, int KB>
+__global__ void __launch_bounds__(kThreads, 1)
+    sp24_gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmA,
+                            const __grid_constant__ CUtensorMap tmB, const SplitParams P) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using C = SplitCfg<DT, BN, KB>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t accf_bar;
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = P.splits;
+  const int rank = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int tile = static_cast<int>(blockIdx.x) / S;
+  const int mb = tile % P.m_blocks;
+  const int nb = tile / P.m_blocks;
+  const int g0 = static_cast<int>(static_cast<long long>(P.stages) * rank / S);
+  const int g1 = static_cast<int>(static_cast<long long>(P.stages) * (rank + 1) / S);
+  const int nst = g1 - g0;
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&accf_bar, 1);
+    mbar_init(&drain_bar, 1);
+    fence_barrier_init();
+    // First use of every slot armed here; the MMA warp re-arms each slot for
+    // its next stage when it sees the slot fill.
+    for (int s = 0; s < C::STAGES && s < nst; ++s)
+      mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, g0 + s));
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  const uint64_t tmo = P.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // Lane l issues copy l of every stage: A boxes, then B boxes, then
+    // metadata atoms.  Coordinates advance by a constant step per stage.
+    if (!P.stall_producer && lane < C::LOADS) {
+      const bool is_a = lane < C::LOADS_A;
+      const bool is_b = !is_a && lane < C::LOADS_A + C::LOADS_B;
+      const int bl = lane - C::LOADS_A;
+      const int el = lane - C::LOADS_A - C::LOADS_B;
+      const int u = is_a ? lane : (is_b ? bl / C::B_BOXES : 0);
+      const uint32_t off = is_a   ? static_cast<uint32_t>(u * C::A_BOX)
+                           : is_b ? static_cast<uint32_t>(C::A_BYTES + u * C::B_UNIT +
+                                                          (bl % C::B_BOXES) * C::B_BOX_BYTES)
+                                  : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + el * kAtomBytes);
+      int x = is_a ? (g0 * KB + u) * C::A_COLS
+                   : (is_b ? nb * BN + (bl % C::B_BOXES) * C::B_BOXN : 0);
+      int y = is_a ? mb * kBlockM : (is_b ? (g0 * KB + u) * C::UK : 0);
+      const int dx = is_a ? KB * C::A_COLS : 0;
+      const int dy = is_b ? C::BKD : 0;
+      int atom = g0 * C::E_S + el;
+      int s = 0;
+      uint32_t ph = 0, soff = 0;
+      uint32_t issued_mask = 0, issued_ph = 0;
+      bool ok = true;
+      for (int i = 0; i < nst; ++i) {
+        int good = 1;
+        if (lane == 0) good = mbar_wait_fast(&empty_bar[s], ph ^ 1u, &abort_sh, tmo) ? 1 : 0;
+        if (__shfl_sync(C::LOAD_LANES, good, 0) == 0) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = smem + soff + off;
+        if (is_a) {
+          tma_load_2d(dst, &tmA, &full_bar[s], x, y);
+        } else if (is_b) {
+          tma_load_2d(dst, &tmB, &full_bar[s], x, y);
+        } else if (atom < P.katoms) {
+          bulk_load(dst, P.meta_tc + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
+                    kAtomBytes, &full_bar[s]);
+        }
+        if (lane == 0) {
+          issued_mask |= 1u << s;
+          issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
+        }
+        x += dx;
+        y += dy;
+        atom += C::E_S;
+        soff += C::STAGE_BYTES;
+        if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
+      }
+      if (!ok && lane == 0) {
+        // Error path: let every copy issued so far land before the CTA exits.
+        volatile int dummy = 0;
+        for (int j = 0; j < C::STAGES; ++j)
+          if (issued_mask & (1u << j)) mbar_wait(&full_bar[j], (issued_ph >> j) & 1u, &dummy, tmo);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t smem_base = smem_u32(smem);
+    const uint64_t adesc0 = make_sdesc(smem_base, 16, 1024, kLayoutSW128);
+    const uint64_t bdesc0 = make_sdesc(smem_base + C::A_BYTES, C::B_LBO, C::B_SBO, C::B_LAYOUT);
+    const uint64_t edesc0 =
+        make_sdesc(smem_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
+    constexpr uint32_t SD = C::STAGE_BYTES >> 4;
+    int s = 0;
+    uint32_t ph = 0, soff = 0, ebuf = 0;
+    bool ok = true, any = false;
+    for (int i = 0; i < nst; ++i) {
+      const int g = g0 + i;
+      if (!mbar_wait_warp(&full_bar[s], ph, &abort_sh, tmo)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0 && i + C::STAGES < nst)
+        mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, g + C::STAGES));
+      tc_fence_after();
+      ebuf ^= static_cast<uint32_t>(C::E_S * 4);
+      const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(BN) + ebuf;
+#pragma unroll
+      for (int a = 0; a < C::E_S; ++a)
+        if (g * C::E_S + a < P.katoms)
+          tc_cp_elect<1>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
+      const int kleft = P.k - g * C::BKD;
+#pragma unroll
+      for (int u = 0; u < KB; ++u)
+#pragma unroll
+        for (int j = 0; j < C::MMAS_U; ++j) {
+          const int kk = u * C::UK + j * C::MMA_K;   // dense K inside the stage
+          if (kk < kleft) {
+            const int atom_in = kk / 128;
+            const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>((kk % 128) / 32)
+                                                : static_cast<uint32_t>(2 * ((kk % 128) / 64));
+            const uint64_t ad = adesc0 + soff + u * (C::A_BOX >> 4) + j * 2;
+            const uint64_t bd =
+                bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4);
+            tc_mma_sp_elect<1, C::KIND>(tmem_base, ad, bd, e_tmem + 4 * atom_in + (col & ~1u),
+                                        C::IDESC | (col & 1u), (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+      any = true;
+      tc_commit_elect<1>(&empty_bar[s], 0);
+      soff += SD;
+      if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
+    }
+    if (ok) tc_commit_elect<1>(&accf_bar, 0);
+    if (!ok && any) {
+      volatile int dummy = 0;
+      tc_commit_elect<1>(&drain_bar, 0);
+      if (lane == 0) mbar_wait(&drain_bar, 0, &dummy, tmo);
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait_sleepy(&accf_bar, 0, &abort_sh, tmo);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok) {
+      tc_fence_after();
+      const int row_l = q * 32 + lane;
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+      float* red = reinterpret_cast<float*>(smem);   // ring is idle once accf has fired
+#pragma unroll 1
+      for (int c = 0; c < BN; c += C::CH) {
+        uint32_t r[C::CH];
+        if constexpr (C::CH == 32) {
+          tmem_ld_x32(tb + c, r);
+        } else {
+          tmem_ld_x16(tb + c, r);
+        }
+        tmem_ld_wait(r);
+        if (S == 1) {
+          store_chunk<C::CH>(P, r, mb * kBlockM + row_l, nb * BN + c);
+        } else {
+#pragma unroll
+          for (int v = 0; v < C::CH; v += 4)
+            *reinterpret_cast<float4*>(red + row_l * C::RS + c + v) =
+                make_float4(__uint_as_float(r[v]), __uint_as_float(r[v + 1]),
+                            __uint_as_float(r[v + 2]), __uint_as_float(r[v + 3]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (S > 1) {
+    // Partials of all ranks are complete and visible after this barrier
+    // (release/acquire at cluster scope).
+    cluster_sync();
+    const int r0 = kBlockM * rank / S;
+    const int r1 = kBlockM * (rank + 1) / S;
+    constexpr int NV = BN / 4;
+    const float* red = reinterpret_cast<const float*>(smem);
+    for (int idx = threadIdx.x; idx < (r1 - r0) * NV; idx += kThreads) {
+      const int rl = r0 + idx / NV;
+      const int cg = idx - (idx / NV) * NV;
+      const uint32_t la = smem_u32(red + rl * C::RS + cg * 4);
+      float4 acc = ld_dsmem_f4(mapa_shared(la, 0));
+      for (int src = 1; src < S; ++src) {
+        const float4 v = ld_dsmem_f4(mapa_shared(la, static_cast<uint32_t>(src)));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      store_vec4(P, acc, mb * kBlockM + rl, nb * BN + cg * 4);
+    }
+    // No CTA leaves (and releases its shared memory) while others still read it.
+    cluster_sync();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && abort_sh != 0 && P.status != nullptr) atomicExch(P.status, 1);
+#endif
+}
+
+}  // namespace sp24

@@ -266,6 +266,15 @@ SP24_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
+// 16-byte load from a cluster shared-memory address (any CTA of the cluster).
+SP24_DEV float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
 SP24_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
@@ -328,8 +337,9 @@ SP24_DEV void tc_mma_sp_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, ui
 // ---------------------------------------------------------------- warp-converged issue
 // The MMA-issuing warp runs its loop with all 32 lanes converged, so every
 // operand below is warp-uniform; inside the asm one lane is elected to issue.
-// Issuing a stage's MMAs from one asm block (instead of one block per MMA in
-// lane-0-only code) doubled the sustained MMA issue rate on sm_100a.
+// A same-box A/B run measured no throughput difference between this form and
+// lane-0-only code with one asm block per MMA; the converged form keeps the
+// issuing warp free of divergent branches around each tcgen05 instruction.
 template <int CG>
 SP24_DEV void tc_cp_elect(uint32_t taddr, uint64_t sdesc) {
   if constexpr (CG == 1) {

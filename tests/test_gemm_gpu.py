@@ -137,7 +137,9 @@ def _decode_case(dt, m, k, seed):
 @pytest.mark.parametrize("dt", [0, 1, 2])
 @pytest.mark.parametrize("kernel,bn,m", [("1sm", 16, 128), ("1sm", 32, 128), ("1sm", 64, 128),
                                          ("1sm", 128, 128), ("1sm", 256, 128),
-                                         ("2sm", 256, 256), ("2sm", 256, 512)])
+                                         ("2sm", 256, 256), ("2sm", 256, 512),
+                                         ("splitk", 16, 128), ("splitk", 64, 256),
+                                         ("splitk", 128, 384)])
 def test_decode_known_answer(dt, kernel, bn, m, monkeypatch):
     """B = identity: C must equal the dense A exactly, so every metadata
     nibble, lane and column of the TMEM image is checked."""
@@ -170,7 +172,7 @@ def test_one_hot_b_every_k_position(dt):
 
 
 @pytest.mark.parametrize("dt", [0, 1, 2])
-@pytest.mark.parametrize("kernel", ["1sm", "2sm"])
+@pytest.mark.parametrize("kernel", ["1sm", "2sm", "splitk"])
 def test_alternating_six_pattern(dt, kernel, monkeypatch):
     """The reference debugging log's signature of a wrong metadata layout is
     'one-hot passes, alternating fails'; the alternating six-pattern A is
@@ -241,6 +243,81 @@ def test_kernels_agree():
         else:
             os.environ["SP24_KERNEL"] = old
     assert (c1 - c2).abs().max().item() <= 1e-5
+
+
+# ------------------------------------------------------------------ narrow N, split K
+SPLITK_CASES = [
+    # m, n, k, K slices, units per stage
+    (256, 8, 4096, 4, 2),
+    (200, 48, 2112, 3, 1),      # ragged M, ragged last stage
+    (128, 128, 1024, 8, 1),
+    (384, 16, 8192, 2, 2),
+    (64, 100, 640, 5, 2),       # ragged N inside a 128-wide tile
+    (130, 32, 256, 1, 2),
+]
+
+
+def _with_env(env, fn):
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        return fn()
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k,splits,kb", SPLITK_CASES)
+def test_splitk_matches_oracle(dt, m, n, k, splits, kb):
+    """The narrow-N kernel with K cut over a cluster of `splits` CTAs and
+    reduced through distributed shared memory: within the row-norm bound of
+    the oracle, bf16 output the rounding of the fp32 output, bit-identical
+    on a repeat call (the reduction order is fixed), and within fp32
+    rounding of the unsplit result."""
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    gen = oracle.Gen(m + 3 * n + k + splits)
+    a, b, a_c, e, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    b_t = to_dev(b, dt)
+    env = {"SP24_KERNEL": "splitk", "SP24_SPLITS": str(splits), "SP24_SPLITK_KB": str(kb)}
+
+    def run():
+        return sp24.gemm(ac_t, e_t, b_t, m, n, k, out_bf16=True, dtype=lib_dtype(dt))
+
+    c, cb = _with_env(env, run)
+    c_again, _ = _with_env(env, run)
+    c_one, _ = _with_env({**env, "SP24_SPLITS": "1"}, run)
+    torch.cuda.synchronize()
+    check_c(c, c_ref, a, b, dt, abs_rule=(k <= 1024))
+    assert torch.equal(cb, c.to(torch.bfloat16))
+    assert torch.equal(c, c_again)
+    scale = c_one.abs().max().item() + 1.0
+    assert (c - c_one).abs().max().item() <= 1e-5 * scale
+
+
+def test_splitk_mlp_shapes_default_dispatch():
+    """Configuration 4's narrow shapes through the default dispatch (W_down:
+    M = 4096, K = 14336, T = 8 splits K; W_up: M = 14336, T = 16 does not),
+    magnitude-pruned N(0, 0.02) weights, checked on 64 seeded rows."""
+    for (m, k, t) in ((4096, 14336, 8), (14336, 4096, 16)):
+        g = torch.Generator(device=DEV).manual_seed(m + t)
+        w = (torch.randn((m, k), device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+        a = sp24.prune_2of4(w)
+        b = torch.randn((k, t), device=DEV, generator=g).to(torch.bfloat16)
+        ac_t, e_t = sp24.compress(a)
+        c, _ = sp24.gemm(ac_t, e_t, b, m, t, k)
+        torch.cuda.synchronize()
+        rows = np.sort(np.random.default_rng(t).choice(m, 64, replace=False))
+        a_bits, b_bits = to_host_bits(a)[rows], to_host_bits(b)
+        ref = oracle.gemm(1, a_bits, b_bits, threads=8)
+        err = oracle.row_norm_rel_error(c[rows].cpu().numpy(), ref, oracle.to_float(1, a_bits),
+                                        oracle.to_float(1, b_bits))
+        assert err <= 1e-2, err
 
 
 # ------------------------------------------------------------------ e4m3 configuration
@@ -340,7 +417,8 @@ def test_bounded_wait_timeout_returns_error_and_context_survives():
     the next GEMM on the same context is correct."""
     import ctypes
     gen = oracle.Gen(13)
-    for kernel, (m, n, k) in (("1sm", (128, 128, 256)), ("2sm", (256, 256, 256))):
+    cases = (("1sm", (128, 128, 256)), ("2sm", (256, 256, 256)), ("splitk", (256, 64, 2048)))
+    for kernel, (m, n, k) in cases:
         a, b, _, _, c_ref = oracle.host_case(gen, 1, m, n, k, False)
         ac_t, e_t = sp24.compress(to_dev(a, 1))
         img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
@@ -350,11 +428,13 @@ def test_bounded_wait_timeout_returns_error_and_context_survives():
         d = sp24.make_desc(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC, c_f32=c,
                            status=status)
         os.environ["SP24_KERNEL"] = kernel
+        os.environ["SP24_SPLITS"] = "4"     # the split-K case waits in a cluster of 4
         try:
             rc = sp24.load().sp24_selftest_timeout(ctypes.byref(d), 2_000_000,
                                                    torch.cuda.current_stream().cuda_stream)
         finally:
             os.environ.pop("SP24_KERNEL", None)
+            os.environ.pop("SP24_SPLITS", None)
         assert rc == 6
         c2, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC)
         check_c(c2, c_ref, a, b, 1)
