@@ -11,6 +11,12 @@ dense-equivalent FLOPs of all ranks / max-over-ranks time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sp24|reference]
                     [--config 2|3|4|5] [--allgather]
+                    [--config 4 --layer up|down --tokens 8|16|64|128|4096]
+
+Configuration 4 (the MLP layers) at T <= 128 tokens is bound by HBM: its
+roofline is reported in GB/s of algorithmic bytes against the measured copy
+bandwidth, and because its operands fit in L2, L2 is cleaned before every
+step and each step is timed alone.
 
 Metric: dense-equivalent TFLOP/s (2MNK/t).  `roofline` compares the kernel
 with the sparse tensor peak derived from the measured dense bf16 peak
@@ -47,11 +53,26 @@ CONFIGS = {
             k=8192, out=("f32", "bf16"), dist="uniform"),
     3: dict(name="e4m3 2:4 GEMM M=N=K=16384, bf16 out x 1/(sA sB) (config 3)", dt=2, m=16384,
             n=16384, k=16384, out=("bf16",), dist="normal_fp8"),
-    4: dict(name="bf16 MLP W_up 14336x4096 x T=4096, magnitude-pruned N(0,0.02) (config 4)",
+    4: dict(name="bf16 MLP {layer} {m}x{k} x T={n}, magnitude-pruned N(0,0.02) (config 4)",
             dt=1, m=14336, n=4096, k=4096, out=("bf16",), dist="mlp"),
     5: dict(name="fp16 2:4 GEMM M=K=32768 per-GPU N-shard 8192 of N=65536 (config 5)", dt=0,
             m=32768, n=8192, k=32768, out=("f32",), dist="normal"),
 }
+
+
+L2_BYTES = 126 << 20
+
+
+def config_for(args):
+    """The workload of --config (and, for configuration 4, --layer / --tokens)."""
+    cfg = dict(CONFIGS[args.config])
+    if args.config == 4:
+        up = args.layer == "up"
+        cfg["m"], cfg["k"] = (14336, 4096) if up else (4096, 14336)
+        cfg["n"] = args.tokens
+        cfg["name"] = cfg["name"].format(layer="W_up/W_gate" if up else "W_down", m=cfg["m"],
+                                         k=cfg["k"], n=cfg["n"])
+    return cfg
 
 
 def log(*a):
@@ -264,10 +285,14 @@ def main():
     ap.add_argument("--allgather", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=10.0)
+    ap.add_argument("--tokens", type=int, default=4096,
+                    help="configuration 4: activation columns T (8, 16, 64, 128 or 4096)")
+    ap.add_argument("--layer", default="up", choices=["up", "down"],
+                    help="configuration 4: W_up/W_gate (14336x4096) or W_down (4096x14336)")
     ap.add_argument("--steps-ref", type=int, default=1)
     ap.add_argument("--warmup-ref", type=int, default=1)
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = config_for(args)
     if args.impl == "reference":
         run_reference_arm(args, cfg)
         return
@@ -309,6 +334,23 @@ def main():
         if world > 1:
             dist.barrier()
 
+    # Inputs and outputs that fit in L2 twice over would be served from L2 on
+    # back-to-back steps; then every step starts from a cleaned L2: a 256 MB
+    # write (evicts everything) followed by a read of the same buffer (leaves
+    # L2 holding clean lines, so the GEMM's own reads pay no write-backs),
+    # and each step is timed alone with its own events.
+    esz = 1 if dt == 2 else 2
+    out_bytes = sum(4 if o == "f32" else 2 for o in cfg["out"]) * m * n
+    in_bytes = m * k // 2 * esz + m * k // 8 + k * n * esz
+    flush_l2 = in_bytes + out_bytes < 2 * L2_BYTES
+    if flush_l2:
+        flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+        flush_out = torch.empty((), device=dev)
+
+    def clean_l2():
+        flush_buf.zero_()
+        torch.sum(flush_buf, dim=0, out=flush_out)
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -318,13 +360,24 @@ def main():
     with ClockSampler(range(torch.cuda.device_count()) if rank == 0 else [local]) as clk:
         torch.cuda.synchronize()
         barrier()
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
+        if flush_l2:
+            evs = []
+            for _ in range(args.steps):
+                clean_l2()
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                step()
+                a1.record(stream)
+                evs.append((a0, a1))
+        else:
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
         torch.cuda.synchronize()
         barrier()
-    ms_local = e0.elapsed_time(e1)
+    ms_local = (sum(a.elapsed_time(b) for a, b in evs) if flush_l2 else e0.elapsed_time(e1))
     if sp24.last_kernel_status() != 0:
         raise SystemExit("sp24: a kernel reported a bounded-wait timeout")
     t = torch.tensor([ms_local], device=dev)
@@ -414,11 +467,28 @@ def main():
         dense_peak, hbm_peak, peak_src = load_peaks()
         peak_scale = 2.0 if dt == 2 else 1.0       # e4m3 issues at twice the 16-bit rate
         sparse_peak = dense_peak * peak_scale * SPARSE_OVER_DENSE
-        out_bytes = sum(4 if o == "f32" else 2 for o in cfg["out"]) * m * n
-        esz = 1 if dt == 2 else 2
-        alg_bytes = m * k // 2 * esz + m * k // 8 + k * n * esz + out_bytes
+        alg_bytes = in_bytes + out_bytes
+        ms_kernel = ms_local / args.steps
+        hbm_bound = args.config == 4 and n <= 128
         tag = {2: "sp24_gemm2sm_bf16_8192", 3: "sp24_gemm2sm_e4m3_16384",
-               4: "sp24_gemm_mlp", 5: "sp24_gemm2sm_f16_32768"}[args.config]
+               4: f"sp24_gemm_mlp_{args.layer}_T{n}", 5: "sp24_gemm2sm_f16_32768"}[args.config]
+        if hbm_bound:
+            gbps = alg_bytes / (ms_kernel * 1e-3) / 1e9
+            roofline = {"bound": "hbm", "achieved": gbps, "peak": hbm_peak, "unit": "GB/s",
+                        "frac": gbps / hbm_peak, "traffic": profile_traffic(tag),
+                        "peak_basis": f"{peak_src} HBM copy bandwidth",
+                        "algorithmic_bytes": alg_bytes, "tflops": kernel_tflops,
+                        "frac_of_sparse_tensor_peak": kernel_tflops / sparse_peak}
+        else:
+            roofline = {"bound": "tensor", "achieved": kernel_tflops, "peak": sparse_peak,
+                        "unit": "TFLOP/s", "frac": kernel_tflops / sparse_peak,
+                        "traffic": profile_traffic(tag),
+                        "peak_basis": f"{peak_src} dense bf16 {dense_peak} TF/s x "
+                                      f"{'2 (e4m3) x ' if dt == 2 else ''}16/9 sparse issue ratio",
+                        "frac_of_nominal_sparse": kernel_tflops / (4500.0 * peak_scale),
+                        "algorithmic_bytes": alg_bytes,
+                        "hbm_GBps_at_alg_bytes": alg_bytes / (ms_kernel * 1e-3) / 1e9,
+                        "hbm_peak_GBps": hbm_peak}
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
@@ -427,17 +497,11 @@ def main():
             "config": {"workload": cfg["name"], "m": m, "n_per_gpu": n, "n_total": n * world,
                        "k": k, "outputs": list(cfg["out"]),
                        "parallelism": f"N-shard x{world}, A + metadata replicated, no collective",
-                       "l2": "no flush: inputs (A_c + metadata + B) exceed the 126 MB L2"},
+                       "l2": ("cleaned before every step (256 MB write, then read); "
+                              "per-step CUDA events" if flush_l2 else
+                              "no flush: inputs + outputs exceed twice the 126 MB L2")},
             "pct_of_sparse_peak": 100.0 * kernel_tflops / sparse_peak,
-            "roofline": {"bound": "tensor", "achieved": kernel_tflops, "peak": sparse_peak,
-                         "unit": "TFLOP/s", "frac": kernel_tflops / sparse_peak,
-                         "traffic": profile_traffic(tag),
-                         "peak_basis": f"{peak_src} dense bf16 {dense_peak} TF/s x "
-                                       f"{'2 (e4m3) x ' if dt == 2 else ''}16/9 sparse issue ratio",
-                         "frac_of_nominal_sparse": kernel_tflops / (4500.0 * peak_scale),
-                         "algorithmic_bytes": alg_bytes,
-                         "hbm_GBps_at_alg_bytes": alg_bytes / (ms_local / args.steps * 1e-3) / 1e9,
-                         "hbm_peak_GBps": hbm_peak},
+            "roofline": roofline,
             "clocks": clk.summary(),
             "gpu_launches": args.steps,
             "e2e": e2e,
