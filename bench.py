@@ -396,19 +396,29 @@ def main():
         flat = c32.reshape(-1)
         out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=dev)
         dist.all_gather_into_tensor(out, flat)
+        full = sp24.unshard_columns_f32(out, m, n * world, world, n)   # warm-up (allocates)
         torch.cuda.synchronize()
         barrier()
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
-        a0.record(stream)
-        dist.all_gather_into_tensor(out, flat)
-        full = sp24.unshard_columns_f32(out, m, n * world, world, n)
-        a1.record(stream)
+        reps = 3
+        marks = []
+        for _ in range(reps):
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a2 = torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            dist.all_gather_into_tensor(out, flat)
+            a1.record(stream)
+            full = sp24.unshard_columns_f32(out, m, n * world, world, n)
+            a2.record(stream)
+            marks.append((a0, a1, a2))
         torch.cuda.synchronize()
-        ta = torch.tensor([a0.elapsed_time(a1)], device=dev)
+        ta = torch.tensor([sum(x.elapsed_time(y) for x, y, _ in marks) / reps,
+                           sum(y.elapsed_time(z) for _, y, z in marks) / reps], device=dev)
         dist.all_reduce(ta, op=dist.ReduceOp.MAX)
-        allgather = {"ms": ta.item(), "bytes_per_rank": flat.numel() * 4 * (world - 1),
-                     "GB_per_s_per_rank": flat.numel() * 4 * (world - 1) / (ta.item() * 1e-3) / 1e9}
+        recv = flat.numel() * 4 * (world - 1)
+        allgather = {"ms": ta[0].item() + ta[1].item(), "nccl_ms": ta[0].item(),
+                     "unshard_ms": ta[1].item(), "bytes_received_per_rank": recv,
+                     "nccl_GB_per_s_per_rank": recv / (ta[0].item() * 1e-3) / 1e9}
         del out, full
 
     # End to end through the public C ABI with host buffers.

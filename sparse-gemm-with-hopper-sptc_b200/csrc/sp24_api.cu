@@ -833,8 +833,11 @@ sp24_status sp24_unshard_columns_f32(const float* src, float* dst, int m, int n,
   sp24_shard_columns(n, world, 0, align, &n0, &n1);
   const int per = std::max(1, n1 - n0);
   cudaStream_t s = as_stream(stream);
-  const long long total = static_cast<long long>(m) * n;
-  sp24::unshard_columns_kernel<<<grid_for(total, 256), 256, 0, s>>>(src, dst, m, n, world, per);
+  const int vec = (per % 4 == 0 && n % 4 == 0 && aligned16(src) && aligned16(dst)) ? 1 : 0;
+  const int per_row = vec ? (n + 3) / 4 : n;
+  const unsigned gx = static_cast<unsigned>(std::min(64, std::max(1, (per_row + 255) / 256)));
+  const unsigned gy = static_cast<unsigned>(std::min(m, 65535));
+  sp24::unshard_columns_kernel<<<dim3(gx, gy), 256, 0, s>>>(src, dst, m, n, world, per, vec);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
 }

@@ -221,15 +221,31 @@ __global__ void quantize_e4m3_kernel(const float* __restrict__ x, size_t n,
 // dst[r][c] = shard(c)[r][c - n0(shard)] where shard r's block starts at
 // element offset m * n0(r) in src.
 __global__ void unshard_columns_kernel(const float* __restrict__ src, float* __restrict__ dst,
-                                       int m, int n, int world, int per) {
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<long long>(m) * n) return;
-  const int r = static_cast<int>(idx / n);
-  const int c = static_cast<int>(idx - static_cast<long long>(r) * n);
-  const int g = min(c / per, world - 1);
-  const int n0 = g * per;
-  const int w = min(per, n - n0);
-  dst[idx] = src[static_cast<long long>(m) * n0 + static_cast<long long>(r) * w + (c - n0)];
+                                       int m, int n, int world, int per, int vec) {
+  // Rows are spread over blockIdx.y, columns over x; with vec every 4-column
+  // group lies inside one shard (per % 4 == 0, n % 4 == 0) and moves as one
+  // 16-byte access.
+  const int step = gridDim.x * blockDim.x;
+  for (int r = blockIdx.y; r < m; r += gridDim.y) {
+    float* drow = dst + static_cast<long long>(r) * n;
+    if (vec) {
+      for (int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x); c < n; c += 4 * step) {
+        const int g = min(c / per, world - 1);
+        const int n0 = g * per;
+        const int w = min(per, n - n0);
+        const float4 v = *reinterpret_cast<const float4*>(
+            src + static_cast<long long>(m) * n0 + static_cast<long long>(r) * w + (c - n0));
+        *reinterpret_cast<float4*>(drow + c) = v;
+      }
+    } else {
+      for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += step) {
+        const int g = min(c / per, world - 1);
+        const int n0 = g * per;
+        const int w = min(per, n - n0);
+        drow[c] = src[static_cast<long long>(m) * n0 + static_cast<long long>(r) * w + (c - n0)];
+      }
+    }
+  }
 }
 
 }  // namespace sp24

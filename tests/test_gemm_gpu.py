@@ -411,6 +411,22 @@ def test_nshard_on_one_gpu_matches_full():
     assert torch.equal(rebuilt, full)
 
 
+@pytest.mark.parametrize("m,n,world,align", [(37, 1001, 3, 8), (64, 1024, 4, 256), (5, 7, 2, 1)])
+def test_unshard_columns_matches_host_permutation(m, n, world, align):
+    """Packed column blocks [rank][m][w_rank] -> row-major C, on the 16-byte
+    path (shards a multiple of 4 wide) and the scalar path (ragged widths)."""
+    rng = np.random.default_rng(m + n)
+    full = rng.standard_normal((m, n)).astype(np.float32)
+    blocks = []
+    for r in range(world):
+        n0, n1 = sp24.shard_columns(n, world, r, align)
+        blocks.append(full[:, n0:n1].reshape(-1))
+    packed = torch.from_numpy(np.concatenate(blocks)).to(DEV)
+    got = sp24.unshard_columns_f32(packed, m, n, world, align)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy(), full)
+
+
 def test_bounded_wait_timeout_returns_error_and_context_survives():
     """A producer that never loads: the MMA / epilogue waits run out after
     2 ms, the kernel frees its TMEM and returns; the status word says so and
