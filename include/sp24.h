@@ -6,7 +6,8 @@
  * A is 2:4-sparse along K and is passed compressed: A_c holds the two kept
  * values of every aligned group of four (M x K/2, row-major) and the metadata
  * holds one 4-bit code per group (i0 | i1 << 2, i0 < i1).  B is dense, K x N,
- * row-major.  Element types: fp16, bf16, fp8 e4m3 (A and B share the type).
+ * row-major.  Element types: fp16, bf16 and fp8 (A and B share the type, except
+ * that the fp8 formats e4m3 and e5m2 may be mixed between A and B).
  *
  * Every entry point is stream-ordered, never exits the process and reports
  * errors through sp24_status.  Pointers are device pointers unless a comment
@@ -58,7 +59,15 @@ typedef enum sp24_status {
 typedef enum sp24_dtype {
   SP24_F16 = 0,   /* reference: half           (RawSparseConfig<half>, :300-309)          */
   SP24_BF16 = 1,  /* reference: __nv_bfloat16  (RawSparseConfig<__nv_bfloat16>, :311-320) */
-  SP24_E4M3 = 2   /* reference: __nv_fp8_e4m3  (RawSparseConfig<__nv_fp8_e4m3>, :322-331) */
+  SP24_E4M3 = 2,  /* reference: __nv_fp8_e4m3  (RawSparseConfig<__nv_fp8_e4m3>, :322-331) */
+  /* Mixed fp8 (kind::f8f6f4 takes independent A and B formats).  The first
+     named format is A's, the second B's; for the single-matrix entry points
+     (compress, prune, repack) the dtype names A's element type.
+     reference: mma.sp ... .f32.e5m2.e4m3.f32, mma_sp_m16n8k64_fp32fp8.cu:197-217
+     (A __nv_fp8_e5m2, B __nv_fp8_e4m3). */
+  SP24_E5M2_E4M3 = 3,
+  SP24_E4M3_E5M2 = 4, /* no reference counterpart */
+  SP24_E5M2 = 5       /* A and B e5m2; no reference counterpart */
 } sp24_dtype;
 
 typedef enum sp24_meta_format {
@@ -84,7 +93,7 @@ typedef struct sp24_gemm_desc {
   float* c_f32;                /* optional fp32 output, m x n, row stride ldc           */
   void* c_bf16;                /* optional bf16 output, m x n, row stride ldc           */
   int64_t ldc;                 /* elements; 0 = n                                       */
-  float alpha;                 /* C = alpha * (A*B); e4m3: 1/(scale_a*scale_b). 0 = 1.0 */
+  float alpha;                 /* C = alpha * (A*B); fp8: 1/(scale_a*scale_b). 0 = 1.0  */
   int tile_n;                  /* 0 = auto; 8..256 selects the reference's BlockN
                                   variant (8 runs on the 16-wide tile)                  */
   void* workspace;             /* device scratch for META_REF repack / B padding        */
@@ -128,7 +137,7 @@ sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, i
 /* The GEMM.  Reference: wgmma_sp_raw_kernel<Element,BlockN>
    (wgmma_sp_raw_common.hpp:955-1030), grid (N/BlockN, M/64) x 128 threads,
    fp32 C.  Preconditions of the reference (M%64, N%BlockN, K%32 / K%64 for
-   e4m3; :1042-1045) are relaxed to: k % 32 == 0 (k % 64 for e4m3), m,n >= 1. */
+   e4m3; :1042-1045) are relaxed to: k % 32 == 0 (k % 64 for fp8), m,n >= 1. */
 sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream);
 
 /* Reads and clears the library-owned device status word that kernels raise
@@ -168,12 +177,18 @@ sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long ti
 #define SP24_NOALLOC_SCRATCH_BYTES (16u << 20)
 sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream);
 
-/* FP8 helpers for the e4m3 path.
+/* FP8 helpers.
    sp24_amax_f32: amax_dev[0] = max |x| over count floats (device).
    sp24_quantize_e4m3: q[i] = e4m3_rn_satfinite(x[i] * scale[0]) with
-   scale[0] = 448 / amax (computed on device from amax_dev). */
+   scale[0] = 448 / amax (computed on device from amax_dev).
+   sp24_quantize_e5m2: the same with e5m2 and scale[0] = 57344 / amax.
+   Reference: quantize_fp8 / quantize_fp8_kernel (RN conversion through the
+   __nv_fp8_* constructors), mma_sp_m16n8k64_fp32fp8.cu:126-130, 341-347; the
+   per-tensor 448/amax scale is the e4m3 benchmark configuration's. */
 sp24_status sp24_amax_f32(const float* x, size_t count, float* amax_dev, sp24_stream_t stream);
 sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_dev,
+                               float* scale_dev, uint8_t* q, sp24_stream_t stream);
+sp24_status sp24_quantize_e5m2(const float* x, size_t count, const float* amax_dev,
                                float* scale_dev, uint8_t* q, sp24_stream_t stream);
 
 /* Multi-GPU N-sharding helpers (no collective on the GEMM path).

@@ -6,7 +6,9 @@ reference's host algorithms, see sp24_oracle.cpp) and, when it was built,
 it lies).  Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
 legs use this module; the product library never does.
 
-Arrays cross as numpy raw bits: uint16 for fp16/bf16, uint8 for e4m3.
+Arrays cross as numpy raw bits: uint16 for fp16/bf16, uint8 for e4m3/e5m2.
+Functions of one matrix take its element code (F16, BF16, E4M3, E5M2); the
+library's mixed fp8 dtypes map to an (A, B) pair of them through ``elems``.
 """
 from __future__ import annotations
 
@@ -20,11 +22,22 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "lib", "libsp24_oracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libsp24ref.so")
+REF_FP8_LIB = os.path.join(HERE, "_ref", "libsp24ref_fp8.so")
 
-F16, BF16, E4M3 = 0, 1, 2
-BITS = {F16: np.uint16, BF16: np.uint16, E4M3: np.uint8}
+F16, BF16, E4M3, E5M2 = 0, 1, 2, 3
+BITS = {F16: np.uint16, BF16: np.uint16, E4M3: np.uint8, E5M2: np.uint8}
 NAMES = {"half": F16, "half_t": F16, "__nv_bfloat16": BF16, "bfloat16_t": BF16,
-         "__nv_fp8_e4m3": E4M3}
+         "__nv_fp8_e4m3": E4M3, "__nv_fp8_e5m2": E5M2}
+
+# Library dtype codes (include/sp24.h) -> (A element, B element).
+LIB_E5M2_E4M3, LIB_E4M3_E5M2, LIB_E5M2 = 3, 4, 5
+_ELEMS = {0: (F16, F16), 1: (BF16, BF16), 2: (E4M3, E4M3), LIB_E5M2_E4M3: (E5M2, E4M3),
+          LIB_E4M3_E5M2: (E4M3, E5M2), LIB_E5M2: (E5M2, E5M2)}
+
+
+def elems(lib_dtype: int):
+    """(A element code, B element code) of a library dtype."""
+    return _ELEMS[lib_dtype]
 
 _o = None
 _r = None
@@ -51,6 +64,8 @@ def lib():
         o.oracle_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
         o.oracle_decompress.argtypes = [c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]
         o.oracle_gemm.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int]
+        o.oracle_gemm_mixed.argtypes = [c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                        c_int, c_int]
         o.oracle_gemm_rows.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                        c_int, c_int]
         o.oracle_count_abs_errors.restype = c_int
@@ -59,6 +74,8 @@ def lib():
         o.oracle_meta_tc_image.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p]
         o.oracle_quantize_e4m3.restype = c_float
         o.oracle_quantize_e4m3.argtypes = [c_void_p, c_size_t, c_void_p]
+        o.oracle_quantize_e5m2.restype = c_float
+        o.oracle_quantize_e5m2.argtypes = [c_void_p, c_size_t, c_void_p]
         o.oracle_to_float.argtypes = [c_int, c_void_p, c_size_t, c_void_p]
         o.oracle_from_float.argtypes = [c_int, c_void_p, c_size_t, c_void_p]
         _o = o
@@ -84,6 +101,33 @@ def ref_lib():
         r.ref_cpu_gemm.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int]
         _r = r
     return _r
+
+
+def ref_fp8_available() -> bool:
+    return os.path.exists(REF_FP8_LIB)
+
+
+def ref_fp8_suite():
+    """Every case of the reference's mixed fp8 entry point
+    (mma_sp_m16n8k64_fp32fp8.cu, run_one), produced by its own host code:
+    dict of per-case arrays a (16x64 e5m2), b (64x8 e4m3, row-major K x N),
+    a_c (16x32), meta (16x8 reference bytes), c (16x8 fp32), plus tags."""
+    r = ctypes.CDLL(REF_FP8_LIB)
+    r.ref_fp8_suite_size.restype = c_int
+    r.ref_fp8_suite.restype = c_int
+    r.ref_fp8_suite.argtypes = [c_void_p] * 5 + [ctypes.c_char_p, c_int]
+    n = r.ref_fp8_suite_size()
+    a = np.empty((n, 16, 64), np.uint8)
+    bt = np.empty((n, 8, 64), np.uint8)
+    ac = np.empty((n, 16, 32), np.uint8)
+    e = np.empty((n, 16, 2), np.uint32)
+    c = np.empty((n, 16, 8), np.float32)
+    tags = ctypes.create_string_buffer(n * 64)
+    got = r.ref_fp8_suite(_p(a), _p(bt), _p(ac), _p(e), _p(c), tags, 64)
+    assert got == n
+    names = [tags.raw[i * 64:(i + 1) * 64].split(b"\0")[0].decode() for i in range(n)]
+    return {"a": a, "b": np.ascontiguousarray(bt.transpose(0, 2, 1)), "a_c": ac,
+            "meta": e.view(np.uint8).reshape(n, 16, 8), "c": c, "tags": names}
 
 
 # ------------------------------------------------------------------ generators
@@ -157,6 +201,17 @@ def gemm(dt: int, a, b, threads: int = 1):
     return c
 
 
+def gemm_mixed(dta: int, dtb: int, a, b, threads: int = 1):
+    """As gemm, with A and B of different element codes (mixed fp8)."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.float32)
+    lib().oracle_gemm_mixed(dta, dtb, _p(a), _p(b), _p(c), m, n, k, threads)
+    return c
+
+
 def gemm_rows(dt: int, a, b, rows):
     """C rows for the given row indices only (sampled verification of big problems)."""
     a = np.ascontiguousarray(a[rows])
@@ -188,6 +243,13 @@ def quantize_e4m3(x):
     x = np.ascontiguousarray(x, np.float32)
     q = np.empty(x.shape, np.uint8)
     s = lib().oracle_quantize_e4m3(_p(x), x.size, _p(q))
+    return q, float(s)
+
+
+def quantize_e5m2(x):
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.empty(x.shape, np.uint8)
+    s = lib().oracle_quantize_e5m2(_p(x), x.size, _p(q))
     return q, float(s)
 
 

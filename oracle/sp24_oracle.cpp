@@ -20,7 +20,7 @@
 // metadata image and the per-tensor e4m3 quantiser.
 //
 // Element encodings cross this ABI as raw bits: uint16_t for fp16/bf16,
-// uint8_t for e4m3.  Conversions use the CUDA headers' host conversions (the
+// uint8_t for e4m3 and e5m2.  Conversions use the CUDA headers' host conversions (the
 // same ones the reference calls, :48-61), compiled by the host compiler.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,7 +36,11 @@
 
 namespace {
 
-enum { DT_F16 = 0, DT_BF16 = 1, DT_E4M3 = 2 };
+// Element codes (one matrix at a time).  e5m2 appears as A of the reference's
+// mixed fp8 entry point (mma_sp_m16n8k64_fp32fp8.cu, A __nv_fp8_e5m2).
+enum { DT_F16 = 0, DT_BF16 = 1, DT_E4M3 = 2, DT_E5M2 = 3 };
+
+__nv_fp8_interpretation_t fp8_kind(int dt) { return dt == DT_E5M2 ? __NV_E5M2 : __NV_E4M3; }
 
 float to_f(int dt, uint32_t bits) {
   if (dt == DT_F16) {
@@ -50,7 +54,7 @@ float to_f(int dt, uint32_t bits) {
     std::memcpy(&f, &w, 4);
     return f;
   }
-  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(bits), __NV_E4M3);
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(bits), fp8_kind(dt));
   return __half2float(__half(h));
 }
 
@@ -63,10 +67,10 @@ uint32_t from_f(int dt, float v) {
     __nv_bfloat16 b = __float2bfloat16(v);
     return static_cast<__nv_bfloat16_raw>(b).x;
   }
-  return __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+  return __nv_cvt_float_to_fp8(v, __NV_SATFINITE, fp8_kind(dt));
 }
 
-int esz(int dt) { return dt == DT_E4M3 ? 1 : 2; }
+int esz(int dt) { return dt >= DT_E4M3 ? 1 : 2; }
 
 uint32_t ld(int dt, const void* p, size_t i) {
   if (esz(dt) == 2) return static_cast<const uint16_t*>(p)[i];
@@ -193,6 +197,7 @@ void oracle_decompress(int dt, const void* a_c, const uint8_t* meta, int m, int 
 // each element unchanged; B is converted to float once and shared.
 static void gemm_rows_f(int dt, const void* a, const float* bf, float* c, int n, int k, int r0,
                         int r1) {
+  // dt: A's element code (B arrives already converted to float).
   std::vector<float> arow(k);
   for (int r = r0; r < r1; ++r) {
     for (int kk = 0; kk < k; ++kk) arow[kk] = to_f(dt, ld(dt, a, static_cast<size_t>(r) * k + kk));
@@ -212,10 +217,12 @@ void oracle_gemm_rows(int dt, const void* a, const void* b, float* c, int m, int
   gemm_rows_f(dt, a, bf.data(), c, n, k, r0, r1);
 }
 
-void oracle_gemm(int dt, const void* a, const void* b, float* c, int m, int n, int k,
-                 int threads) {
+// A and B of different element codes (the mixed fp8 pairs); same arithmetic.
+void oracle_gemm_mixed(int dta, int dtb, const void* a, const void* b, float* c, int m, int n,
+                       int k, int threads) {
   std::vector<float> bf(static_cast<size_t>(k) * n);
-  for (size_t i = 0; i < bf.size(); ++i) bf[i] = to_f(dt, ld(dt, b, i));
+  for (size_t i = 0; i < bf.size(); ++i) bf[i] = to_f(dtb, ld(dtb, b, i));
+  const int dt = dta;
   if (threads <= 1) {
     gemm_rows_f(dt, a, bf.data(), c, n, k, 0, m);
     return;
@@ -228,6 +235,11 @@ void oracle_gemm(int dt, const void* a, const void* b, float* c, int m, int n, i
     pool.emplace_back(gemm_rows_f, dt, a, bf.data(), c, n, k, r0, r1);
   }
   for (auto& th : pool) th.join();
+}
+
+void oracle_gemm(int dt, const void* a, const void* b, float* c, int m, int n, int k,
+                 int threads) {
+  oracle_gemm_mixed(dt, dt, a, b, c, m, n, k, threads);
 }
 
 int oracle_count_abs_errors(const float* got, const float* ref, size_t count, float atol) {
@@ -269,7 +281,7 @@ void oracle_meta_tc_image(int dt, const uint8_t* meta, int m, int k, uint32_t* i
       for (int L = 0; L < 128; ++L)
         for (int w = 0; w < 4; ++w) {
           uint32_t word = 0;
-          if (dt == DT_E4M3) {
+          if (esz(dt) == 1) {
             const int row = mb * 128 + L, b0 = ka * 16 + 4 * w;
             if (row < m && b0 < rb) {
               const uint8_t* s = meta + static_cast<size_t>(row) * rb + b0;
@@ -294,13 +306,20 @@ void oracle_meta_tc_image(int dt, const uint8_t* meta, int m, int k, uint32_t* i
         }
 }
 
-// Per-tensor e4m3 quantisation: scale = 448 / amax, q = e4m3_rn_satfinite(x * scale).
-float oracle_quantize_e4m3(const float* x, size_t count, uint8_t* q) {
+// Per-tensor fp8 quantisation: scale = largest finite value / amax (448 for
+// e4m3, 57344 for e5m2), q = fp8_rn_satfinite(x * scale).
+static float quantize_fp8(int dt, float max_finite, const float* x, size_t count, uint8_t* q) {
   float amax = 0.0f;
   for (size_t i = 0; i < count; ++i) amax = std::max(amax, std::fabs(x[i]));
-  const float s = amax > 0.0f ? 448.0f / amax : 1.0f;
-  for (size_t i = 0; i < count; ++i) q[i] = static_cast<uint8_t>(from_f(DT_E4M3, x[i] * s));
+  const float s = amax > 0.0f ? max_finite / amax : 1.0f;
+  for (size_t i = 0; i < count; ++i) q[i] = static_cast<uint8_t>(from_f(dt, x[i] * s));
   return s;
+}
+float oracle_quantize_e4m3(const float* x, size_t count, uint8_t* q) {
+  return quantize_fp8(DT_E4M3, 448.0f, x, count, q);
+}
+float oracle_quantize_e5m2(const float* x, size_t count, uint8_t* q) {
+  return quantize_fp8(DT_E5M2, 57344.0f, x, count, q);
 }
 
 // Element conversions for the test harness (bits <-> float).

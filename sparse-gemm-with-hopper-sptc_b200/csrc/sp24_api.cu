@@ -44,8 +44,17 @@ static __device__ __align__(256) uint8_t g_sp24_noalloc_scratch[SP24_NOALLOC_SCR
 
 inline cudaStream_t as_stream(sp24_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
-inline int esize(sp24_dtype dt) { return dt == SP24_E4M3 ? 1 : 2; }
-inline bool dtype_ok(int dt) { return dt == SP24_F16 || dt == SP24_BF16 || dt == SP24_E4M3; }
+inline bool is_fp8(int dt) { return dt >= SP24_E4M3 && dt <= SP24_E5M2; }
+inline int esize(sp24_dtype dt) { return is_fp8(dt) ? 1 : 2; }
+inline bool dtype_ok(int dt) { return dt == SP24_F16 || dt == SP24_BF16 || is_fp8(dt); }
+// kind::f8f6f4 format fields of the instruction descriptor (e4m3 = 0,
+// e5m2 = 1; A at bit 7, B at bit 10).  One set of fp8 kernels serves every
+// pairing; 16-bit types carry their format in the kernel's own constant.
+inline uint32_t idesc_ab(int dt) {
+  const uint32_t a = (dt == SP24_E5M2_E4M3 || dt == SP24_E5M2) ? 1u : 0u;
+  const uint32_t b = (dt == SP24_E4M3_E5M2 || dt == SP24_E5M2) ? 1u : 0u;
+  return is_fp8(dt) ? (a << 7) | (b << 10) : 0u;
+}
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
@@ -136,6 +145,7 @@ struct Prepared {
   void* c_bf16;
   int64_t ldc;
   float alpha;
+  uint32_t idesc_ab;
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -181,6 +191,7 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
   P.ldc = p.ldc;
   P.alpha = p.alpha;
+  P.idesc_ab = p.idesc_ab;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -246,6 +257,7 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
   P.ldc = p.ldc;
   P.alpha = p.alpha;
+  P.idesc_ab = p.idesc_ab;
   P.vec_f32 = p.c_f32 == nullptr                            ? 0
               : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
               : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
@@ -357,6 +369,7 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
   P.ldc = p.ldc;
   P.alpha = p.alpha;
+  P.idesc_ab = p.idesc_ab;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -500,7 +513,7 @@ sp24_status validate(const sp24_gemm_desc* d) {
   if (!dtype_ok(d->dtype)) return SP24_ERR_ARG;
   if (d->meta_format != SP24_META_REF && d->meta_format != SP24_META_TC) return SP24_ERR_ARG;
   if (d->m <= 0 || d->n <= 0 || d->k <= 0) return SP24_ERR_SHAPE;
-  const int kq = d->dtype == SP24_E4M3 ? 64 : 32;
+  const int kq = is_fp8(d->dtype) ? 64 : 32;
   if (d->k % kq != 0) return SP24_ERR_SHAPE;
   if (d->a_c == nullptr || d->meta == nullptr || d->b == nullptr) return SP24_ERR_ARG;
   if (d->c_f32 == nullptr && d->c_bf16 == nullptr) return SP24_ERR_ARG;
@@ -540,6 +553,7 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   p.c_bf16 = d->c_bf16;
   p.ldc = d->ldc ? d->ldc : d->n;
   p.alpha = d->alpha == 0.0f ? 1.0f : d->alpha;
+  p.idesc_ab = idesc_ab(d->dtype);
   p.status = d->status_dev ? d->status_dev : di->status_word;
   p.timeout_ns = timeout_ns;
   p.stall_producer = stall;
@@ -772,14 +786,14 @@ sp24_status sp24_prune_2of4(sp24_dtype dtype, const void* a, int m, int k, int64
 sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, int k,
                              uint8_t* meta_tc, sp24_stream_t stream) {
   if (!dtype_ok(dtype) || meta_ref == nullptr || meta_tc == nullptr) return SP24_ERR_ARG;
-  if (m <= 0 || k <= 0 || k % (dtype == SP24_E4M3 ? 64 : 32) != 0) return SP24_ERR_SHAPE;
+  if (m <= 0 || k <= 0 || k % (is_fp8(dtype) ? 64 : 32) != 0) return SP24_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(meta_tc) & 3u) != 0) return SP24_ERR_ALIGN;
   const int mb = meta_mblocks(m);
   const int ka = meta_katoms(k);
   const long long total = static_cast<long long>(ka) * mb * 128 * 4;
   cudaStream_t s = as_stream(stream);
   sp24::repack_meta_kernel<<<grid_for(total, 256), 256, 0, s>>>(
-      meta_ref, m, k, dtype == SP24_E4M3 ? 1 : 0, reinterpret_cast<uint32_t*>(meta_tc), mb, ka);
+      meta_ref, m, k, is_fp8(dtype) ? 1 : 0, reinterpret_cast<uint32_t*>(meta_tc), mb, ka);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
 }
@@ -799,8 +813,12 @@ sp24_status sp24_amax_f32(const float* x, size_t count, float* amax_dev, sp24_st
   return SP24_OK;
 }
 
-sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_dev,
-                               float* scale_dev, uint8_t* q, sp24_stream_t stream) {
+}  // extern "C"
+
+namespace {
+template <int E5M2>
+sp24_status quantize_fp8(const float* x, size_t count, const float* amax_dev, float* scale_dev,
+                         uint8_t* q, sp24_stream_t stream) {
   if (x == nullptr || amax_dev == nullptr || q == nullptr) return SP24_ERR_ARG;
   if (count == 0) return SP24_OK;
   DeviceInfo* di = nullptr;
@@ -809,9 +827,22 @@ sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_d
   cudaStream_t s = as_stream(stream);
   const unsigned int g = std::min<unsigned int>(grid_for(static_cast<long long>(count), 256),
                                                 static_cast<unsigned int>(di->sm_count) * 16u);
-  sp24::quantize_e4m3_kernel<<<g, 256, 0, s>>>(x, count, amax_dev, scale_dev, q);
+  sp24::quantize_fp8_kernel<E5M2><<<g, 256, 0, s>>>(x, count, amax_dev, scale_dev, q);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
+}
+}  // namespace
+
+extern "C" {
+
+sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_dev,
+                               float* scale_dev, uint8_t* q, sp24_stream_t stream) {
+  return quantize_fp8<0>(x, count, amax_dev, scale_dev, q, stream);
+}
+
+sp24_status sp24_quantize_e5m2(const float* x, size_t count, const float* amax_dev,
+                               float* scale_dev, uint8_t* q, sp24_stream_t stream) {
+  return quantize_fp8<1>(x, count, amax_dev, scale_dev, q, stream);
 }
 
 void sp24_shard_columns(int n, int world, int rank, int align, int* n0, int* n1) {

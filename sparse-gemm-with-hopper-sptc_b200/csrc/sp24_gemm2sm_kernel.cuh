@@ -51,6 +51,8 @@ struct PairParams {
   float* c_f32;
   __nv_bfloat16* c_bf16;
   long long ldc;
+  uint32_t idesc_ab;  // A / B format fields of the instruction descriptor for mixed fp8
+                      // (A at bit 7, B at bit 10; e5m2 = 1), 0 otherwise
   float alpha;
   int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
   int vec_bf16;
@@ -330,7 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(kin)
                                               : static_cast<uint32_t>(2 * kin);
           ecol[sb][j] = 4u * static_cast<uint32_t>(koff / 128) + (col & ~1u);
-          isel[sb][j] = C::IDESC | (col & 1u);
+          isel[sb][j] = C::IDESC | P.idesc_ab | (col & 1u);
         }
       (void)kPerAtom;
       int s = 0;

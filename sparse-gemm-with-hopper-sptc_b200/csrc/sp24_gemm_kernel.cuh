@@ -50,6 +50,8 @@ struct GemmParams {
   float* c_f32;
   __nv_bfloat16* c_bf16;
   long long ldc;
+  uint32_t idesc_ab;  // A / B format fields of the instruction descriptor for mixed fp8
+                      // (A at bit 7, B at bit 10; e5m2 = 1), 0 otherwise
   float alpha;
   int vec_f32;   // 16-byte vector stores allowed for c_f32
   int vec_bf16;  // 16-byte vector stores allowed for c_bf16
@@ -300,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(sub * C::MMAS + j)
                                                 : static_cast<uint32_t>(2 * j);
             ecol[j] = e_tmem + (col & ~1u);
-            isel[j] = C::IDESC | (col & 1u);
+            isel[j] = C::IDESC | P.idesc_ab | (col & 1u);
             ad[j] = adesc0 + soff + j * 2;
             bd[j] = bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4);
           }

@@ -50,6 +50,8 @@ struct SplitParams {
   float* c_f32;
   __nv_bfloat16* c_bf16;
   long long ldc;
+  uint32_t idesc_ab;  // A / B format fields of the instruction descriptor for mixed fp8
+                      // (A at bit 7, B at bit 10; e5m2 = 1), 0 otherwise
   float alpha;
   int vec_f32;
   int vec_bf16;
@@ -315,7 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t bd =
                 bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4);
             tc_mma_sp_elect<1, C::KIND>(tmem_base, ad, bd, e_tmem + 4 * atom_in + (col & ~1u),
-                                        C::IDESC | (col & 1u), (i > 0 || kk > 0) ? 1u : 0u);
+                                        C::IDESC | P.idesc_ab | (col & 1u),
+                                        (i > 0 || kk > 0) ? 1u : 0u);
           }
         }
       any = true;

@@ -4,7 +4,7 @@
 //               wgmma_sp_raw_common.hpp:140-205)
 //   prune      magnitude 2-of-4 pruning (no reference counterpart)
 //   repack     reference metadata -> tcgen05 TMEM image
-//   amax / quantize   per-tensor e4m3 scaling (reference: quantize_fp8_kernel,
+//   amax / quantize   per-tensor fp8 scaling (reference: quantize_fp8_kernel,
 //              mma_sp_m16n8k64_fp32fp8.cu:341-347, and the per-tensor
 //              448/amax scale of the e4m3 benchmark configuration)
 //   unshard    column-block -> row-major permute after a C all-gather
@@ -27,7 +27,10 @@ __device__ __forceinline__ bool nz_bits(uint32_t v) {
   else return (v & 0x7Fu) != 0;
 }
 
-// |x| as float, for the magnitude pruner.  dt: 0 f16, 1 bf16, 2 e4m3.
+// Magnitude key for the pruner.  dt: 0 f16, 1 bf16, 2 any fp8 (e4m3, e5m2).
+// The fp8 formats are sign-magnitude with the exponent above the mantissa, so
+// the seven magnitude bits order exactly like |x| (finite values): the key is
+// those bits, which serves both formats.
 template <int DT>
 __device__ __forceinline__ float mag_bits(uint32_t v) {
   if constexpr (DT == 0) {
@@ -35,8 +38,7 @@ __device__ __forceinline__ float mag_bits(uint32_t v) {
   } else if constexpr (DT == 1) {
     return fabsf(__uint_as_float(v << 16));
   } else {
-    __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
-    return fabsf(__half2float(__half(h)));
+    return static_cast<float>(v & 0x7Fu);
   }
 }
 
@@ -207,15 +209,20 @@ __global__ void amax_kernel(const float* __restrict__ x, size_t n, float* __rest
   }
 }
 
-__global__ void quantize_e4m3_kernel(const float* __restrict__ x, size_t n,
-                                     const float* __restrict__ amax, float* __restrict__ scale_out,
-                                     uint8_t* __restrict__ q) {
+// Per-tensor fp8 quantisation: scale = largest finite value / amax
+// (448 for e4m3, 57344 for e5m2), q = fp8_rn_satfinite(x * scale).
+template <int E5M2>
+__global__ void quantize_fp8_kernel(const float* __restrict__ x, size_t n,
+                                    const float* __restrict__ amax, float* __restrict__ scale_out,
+                                    uint8_t* __restrict__ q) {
+  constexpr float kMax = E5M2 ? 57344.0f : 448.0f;
+  constexpr __nv_fp8_interpretation_t kFmt = E5M2 ? __NV_E5M2 : __NV_E4M3;
   const float am = amax[0];
-  const float s = am > 0.f ? 448.0f / am : 1.0f;
+  const float s = am > 0.f ? kMax / am : 1.0f;
   if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out != nullptr) scale_out[0] = s;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    q[i] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(x[i] * s, __NV_SATFINITE, __NV_E4M3));
+    q[i] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(x[i] * s, __NV_SATFINITE, kFmt));
 }
 
 // dst[r][c] = shard(c)[r][c - n0(shard)] where shard r's block starts at

@@ -21,6 +21,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libsp24.so")
 
 F16, BF16, E4M3 = 0, 1, 2
+# Mixed fp8: A's format first, B's second (kind::f8f6f4 formats may differ).
+E5M2_E4M3, E4M3_E5M2, E5M2 = 3, 4, 5
 META_REF, META_TC = 0, 1
 
 STATUS = {
@@ -35,7 +37,7 @@ EXPORTS = [
     "sp24_gemm_workspace_bytes", "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta",
     "sp24_gemm", "sp24_last_kernel_status", "sp24_selftest_timeout", "sp24_amax_f32",
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
-    "sp24_gemm_noalloc",
+    "sp24_gemm_noalloc", "sp24_quantize_e5m2",
 ]
 
 
@@ -89,6 +91,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_amax_f32.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p]
     lib.sp24_quantize_e4m3.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
                                        c_void_p]
+    lib.sp24_quantize_e5m2.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
+                                       c_void_p]
     lib.sp24_shard_columns.restype = None
     lib.sp24_shard_columns.argtypes = [c_int, c_int, c_int, c_int, POINTER(c_int),
                                        POINTER(c_int)]
@@ -96,7 +100,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                              c_void_p]
     for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_selftest_timeout", "sp24_last_kernel_status",
                  "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_amax_f32",
-                 "sp24_quantize_e4m3", "sp24_unshard_columns_f32", "sp24_check_device"):
+                 "sp24_quantize_e4m3", "sp24_quantize_e5m2", "sp24_unshard_columns_f32",
+                 "sp24_check_device"):
         getattr(lib, name).restype = c_int
     _lib = lib
     return lib
@@ -119,7 +124,13 @@ def _stream(stream) -> int:
 
 
 def dtype_code(tdtype) -> int:
+    """Library dtype of a torch dtype (uint8 = e4m3 bits); ints pass through
+    (the mixed fp8 codes cannot be told from one tensor)."""
     import torch
+    if isinstance(tdtype, int):
+        return tdtype
+    if tdtype == torch.float8_e5m2:
+        return E5M2
     if tdtype == torch.float16:
         return F16
     if tdtype == torch.bfloat16:
@@ -133,8 +144,10 @@ def meta_tc_bytes(m: int, k: int) -> int:
     return int(load().sp24_meta_tc_bytes(m, k))
 
 
-def compress(a_dense, stream=None):
-    """Dense 2:4 A (m x k, CUDA) -> (A_c m x k/2, reference metadata m x k/8 uint8)."""
+def compress(a_dense, stream=None, dtype=None):
+    """Dense 2:4 A (m x k, CUDA) -> (A_c m x k/2, reference metadata m x k/8 uint8).
+    dtype: library dtype code when the tensor's own dtype does not say it
+    (fp8 bits held as uint8)."""
     import torch
     lib = load()
     m, k = a_dense.shape
@@ -142,7 +155,8 @@ def compress(a_dense, stream=None):
     meta = torch.empty((m, k // 8), dtype=torch.uint8, device=a_dense.device)
     bad_dev = torch.empty(1, dtype=torch.int64, device=a_dense.device)
     bad = c_longlong(-1)
-    code = lib.sp24_compress(dtype_code(a_dense.dtype), _ptr(a_dense), m, k, a_dense.stride(0),
+    code = lib.sp24_compress(dtype_code(dtype if dtype is not None else a_dense.dtype),
+                             _ptr(a_dense), m, k, a_dense.stride(0),
                              _ptr(a_c), a_c.stride(0), _ptr(meta), _ptr(bad_dev),
                              ctypes.byref(bad), _stream(stream))
     if code == 3:
@@ -153,12 +167,13 @@ def compress(a_dense, stream=None):
     return a_c, meta
 
 
-def prune_2of4(a, stream=None):
+def prune_2of4(a, stream=None, dtype=None):
     import torch
     lib = load()
     m, k = a.shape
     out = torch.empty_like(a)
-    _check(lib.sp24_prune_2of4(dtype_code(a.dtype), _ptr(a), m, k, a.stride(0), _ptr(out),
+    code = dtype_code(dtype if dtype is not None else a.dtype)
+    _check(lib.sp24_prune_2of4(code, _ptr(a), m, k, a.stride(0), _ptr(out),
                                out.stride(0), _stream(stream)), "sp24_prune_2of4")
     return out
 
@@ -220,8 +235,9 @@ def last_kernel_status(stream=None) -> int:
     return int(load().sp24_last_kernel_status(_stream(stream)))
 
 
-def amax_quantize_e4m3(x, stream=None):
-    """fp32 CUDA tensor -> (e4m3 bits as uint8, scale tensor[1]) with scale = 448/amax."""
+def amax_quantize_e4m3(x, stream=None, e5m2=False):
+    """fp32 CUDA tensor -> (fp8 bits as uint8, scale tensor[1]) with scale =
+    448/amax (e4m3) or 57344/amax (e5m2)."""
     import torch
     lib = load()
     amax = torch.empty(1, dtype=torch.float32, device=x.device)
@@ -229,9 +245,14 @@ def amax_quantize_e4m3(x, stream=None):
     q = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
     s = _stream(stream)
     _check(lib.sp24_amax_f32(_ptr(x), x.numel(), _ptr(amax), s), "sp24_amax_f32")
-    _check(lib.sp24_quantize_e4m3(_ptr(x), x.numel(), _ptr(amax), _ptr(scale), _ptr(q), s),
-           "sp24_quantize_e4m3")
+    fn = lib.sp24_quantize_e5m2 if e5m2 else lib.sp24_quantize_e4m3
+    _check(fn(_ptr(x), x.numel(), _ptr(amax), _ptr(scale), _ptr(q), s),
+           "sp24_quantize_e5m2" if e5m2 else "sp24_quantize_e4m3")
     return q, scale
+
+
+def amax_quantize_e5m2(x, stream=None):
+    return amax_quantize_e4m3(x, stream, e5m2=True)
 
 
 def shard_columns(n: int, world: int, rank: int, align: int):

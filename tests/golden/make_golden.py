@@ -12,7 +12,10 @@ code (oracle/_ref/libsp24ref.so) and records:
     the smallest random case, in golden.npz
 
 plus known-answer compressions of an alternating six-pattern matrix for each
-dtype (pins the e4m3 nibble table of wgmma_sp_raw_common.hpp:176-193).
+dtype (pins the e4m3 nibble table of wgmma_sp_raw_common.hpp:176-193), and
+every case of the reference's mixed fp8 entry point mma_sp_m16n8k64_fp32fp8.cu
+(A e5m2, B e4m3; through oracle/_ref/libsp24ref_fp8.so): dense A, B (row-major
+K x N), A_c, metadata bytes and its fp32 CPU GEMM.
 The CuTe harness (wgmma_sp_demo_common.hpp) shares these host algorithms;
 its suites are recorded the same way.
 
@@ -101,8 +104,19 @@ def main() -> None:
         arrays[f"kat/alternating6_dt{dt}/meta"] = e
         arrays[f"kat/alternating6_dt{dt}/a_c"] = ac
 
+    # The reference's mixed fp8 entry point (A e5m2, B e4m3, 16 x 8 x 64):
+    # every case of its run_one(), through its own host code.
+    legacy_fp8 = None
+    if oracle.ref_fp8_available():
+        s = oracle.ref_fp8_suite()
+        for key in ("a", "b", "a_c", "meta", "c"):
+            arrays[f"legacy_fp8/{key}"] = s[key]
+        legacy_fp8 = {"entry": "mma_sp_m16n8k64_fp32fp8.cu", "seed": 123, "m": 16, "n": 8,
+                      "k": 64, "a": "e5m2", "b": "e4m3", "tags": s["tags"],
+                      "sha256": {key: sha(s[key]) for key in ("a", "b", "a_c", "meta", "c")}}
+
     out = {"generator": "tests/golden/make_golden.py", "reference_seed": 1234,
-           "suites": suites, "kats": kats}
+           "suites": suites, "kats": kats, "legacy_fp8": legacy_fp8}
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(out, f, indent=1)
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)

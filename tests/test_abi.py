@@ -66,6 +66,10 @@ def _desc(**kw):
     (dict(a_c=0), 8),
     (dict(c_f32=0), 8),                    # no output at all
     (dict(dtype=7), 8),
+    (dict(dtype=6), 8),                    # past the last mixed fp8 code
+    (dict(dtype=3, k=96), 1),              # mixed fp8 (e5m2 x e4m3) needs k % 64
+    (dict(dtype=4, k=32), 1),
+    (dict(dtype=5, k=160), 1),
     (dict(a_c=0x10008), 2),                # A_c not 16-byte aligned
     (dict(lda_c=68), 2),                   # A_c row pitch not a multiple of 16 bytes
     (dict(lda_c=32), 1),                   # pitch smaller than k/2

@@ -347,6 +347,70 @@ def test_e4m3_quantize_and_scaled_gemm():
     assert err <= TOL[2], err
 
 
+# ------------------------------------------------------------------ mixed fp8
+def test_legacy_fp8_suite_on_gpu(golden):
+    """Every case of the reference's mixed fp8 entry point
+    (mma_sp_m16n8k64_fp32fp8.cu: A e5m2, B e4m3, 16 x 8 x 64) from the
+    recorded fixtures: GPU compression bit-exact against the reference's,
+    and C equal to its CPU GEMM within 1e-3 (fp8 products are exact in fp32;
+    only the summation order differs)."""
+    _, arrays = golden
+    a_all, b_all = arrays["legacy_fp8/a"], arrays["legacy_fp8/b"]
+    for i in range(a_all.shape[0]):
+        a = torch.from_numpy(a_all[i].copy()).to(DEV)
+        ac_t, e_t = sp24.compress(a, dtype=sp24.E5M2_E4M3)
+        np.testing.assert_array_equal(ac_t.cpu().numpy(), arrays["legacy_fp8/a_c"][i])
+        np.testing.assert_array_equal(e_t.cpu().numpy(), arrays["legacy_fp8/meta"][i])
+        b = torch.from_numpy(b_all[i].copy()).to(DEV)
+        c, _ = sp24.gemm(ac_t, e_t, b, 16, 8, 64, dtype=sp24.E5M2_E4M3)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(c.cpu().numpy(), arrays["legacy_fp8/c"][i], rtol=0, atol=1e-3)
+
+
+def _fp8_case(lib_dt, m, n, k, seed):
+    ea, eb = oracle.elems(lib_dt)
+    rng = np.random.default_rng(seed)
+    pat = rng.integers(0, 6, size=(m, k // 4))
+    vals = rng.uniform(0.25, 2.0, size=(m, k // 4, 2)) * rng.choice([-1, 1], size=(m, k // 4, 2))
+    af = np.zeros((m, k // 4, 4), np.float32)
+    np.put_along_axis(af, np.array(PAIRS)[pat], vals.astype(np.float32), axis=2)
+    a = oracle.from_float(ea, af.reshape(m, k))
+    b = oracle.from_float(eb, rng.uniform(-2, 2, size=(k, n)).astype(np.float32))
+    return a, b, oracle.gemm_mixed(ea, eb, a, b), ea, eb
+
+
+@pytest.mark.parametrize("lib_dt", [3, 4, 5])
+@pytest.mark.parametrize("m,n,k,kernel", [(256, 256, 512, "2sm"), (256, 256, 512, "1sm"),
+                                          (200, 40, 1024, "splitk"), (130, 8, 256, "")])
+def test_mixed_fp8_pairs_match_oracle(lib_dt, m, n, k, kernel):
+    """e5m2 x e4m3, e4m3 x e5m2 and e5m2 x e5m2 on every kernel: the A / B
+    format fields of the instruction descriptor follow the dtype."""
+    a, b, ref, ea, eb = _fp8_case(lib_dt, m, n, k, seed=lib_dt * 100 + n)
+    ac_t, e_t = sp24.compress(to_dev(a, 2), dtype=lib_dt)
+    env = {"SP24_KERNEL": kernel} if kernel else {}
+
+    def run():
+        return sp24.gemm(ac_t, e_t, to_dev(b, 2), m, n, k, dtype=lib_dt)
+
+    c, _ = _with_env(env, run) if env else run()
+    torch.cuda.synchronize()
+    got = c.cpu().numpy()
+    err = oracle.row_norm_rel_error(got, ref, oracle.to_float(ea, a), oracle.to_float(eb, b))
+    assert err <= TOL[2], err
+    assert oracle.count_abs_errors(got, ref, 1e-2) == 0
+
+
+def test_e5m2_quantize_and_prune_match_oracle():
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((256, 512)).astype(np.float32)
+    q, s = sp24.amax_quantize_e5m2(torch.from_numpy(x).to(DEV))
+    q_ref, s_ref = oracle.quantize_e5m2(x)
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref)
+    assert s.item() == pytest.approx(s_ref)
+    pruned = sp24.prune_2of4(q, dtype=sp24.E5M2)
+    np.testing.assert_array_equal(pruned.cpu().numpy(), oracle.prune_2of4(oracle.E5M2, q_ref))
+
+
 # ------------------------------------------------------------------ full-size properties
 def test_config2_bf16_8192_sampled_rows():
     """Benchmark configuration 2 at full size (bf16 8192^3, U(-1,1), uniform

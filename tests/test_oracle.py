@@ -156,3 +156,48 @@ def test_abs_error_count_and_row_norm_metric():
     a = np.ones((2, 4), np.float32)
     b = np.ones((4, 3), np.float32)
     assert oracle.row_norm_rel_error(got, ref, a, b) == pytest.approx(0.02 / (2 * 2 / 2))
+
+
+# ------------------------------------------------------------------ mixed fp8 (e5m2 x e4m3)
+def test_e5m2_decode_is_the_top_byte_of_fp16():
+    """e5m2 shares fp16's sign and exponent layout: its bits << 8 are the fp16 bits."""
+    bits = np.arange(256, dtype=np.uint8)
+    want = (bits.astype(np.uint16) << 8).view(np.float16).astype(np.float32)
+    got = oracle.to_float(oracle.E5M2, bits)
+    finite = np.isfinite(want)
+    np.testing.assert_array_equal(got[finite], want[finite])
+    assert np.isnan(got[~finite & np.isnan(want)]).all()
+
+
+def test_legacy_fp8_suite_matches_reference(golden):
+    """Every case of the reference's mixed fp8 entry point
+    (mma_sp_m16n8k64_fp32fp8.cu: A e5m2, B e4m3, 16 x 8 x 64), recorded from
+    its own host code: the oracle's compression (values and metadata words)
+    and its fp32 GEMM on e5m2 x e4m3 are bit-exact."""
+    meta, arrays = golden
+    info = meta["legacy_fp8"]
+    assert info is not None and len(info["tags"]) == 22
+    a, b = arrays["legacy_fp8/a"], arrays["legacy_fp8/b"]
+    for i in range(a.shape[0]):
+        ac, e = oracle.compress(oracle.E5M2, a[i])
+        np.testing.assert_array_equal(ac, arrays["legacy_fp8/a_c"][i])
+        np.testing.assert_array_equal(e, arrays["legacy_fp8/meta"][i])
+        c = oracle.gemm_mixed(oracle.E5M2, oracle.E4M3, a[i], b[i])
+        np.testing.assert_array_equal(c.view(np.uint32), arrays["legacy_fp8/c"][i].view(np.uint32))
+
+
+@pytest.mark.skipif(not oracle.ref_fp8_available(), reason="reference checkout not built here")
+def test_legacy_fp8_fixtures_match_a_fresh_reference_run(golden):
+    _, arrays = golden
+    s = oracle.ref_fp8_suite()
+    for key in ("a", "b", "a_c", "meta", "c"):
+        np.testing.assert_array_equal(s[key], arrays[f"legacy_fp8/{key}"])
+
+
+def test_quantize_e5m2_scale_and_saturation():
+    x = np.array([[0.0, 1.0, -3.5, 1e-9], [7.0, -7.0, 2.0, 0.25]], np.float32)
+    q, s = oracle.quantize_e5m2(x)
+    assert s == pytest.approx(57344.0 / 7.0)
+    back = oracle.to_float(oracle.E5M2, q) / s
+    assert abs(back[1, 0] - 7.0) < 1e-6 and abs(back[1, 1] + 7.0) < 1e-6
+    assert q[0, 0] == 0
