@@ -177,6 +177,37 @@ sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long ti
 #define SP24_NOALLOC_SCRATCH_BYTES (16u << 20)
 sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream);
 
+/* Fused epilogues (no counterpart in the reference; they replace a second
+   GEMM and an elementwise kernel that callers of the reference run after it).
+   With A the weights (output features along M) and B the activations (tokens
+   along N), per output row r:
+     plain:  C = act(alpha * A B + bias[r])
+     gated:  C = act(alpha * A B + bias[r]) * (alpha_up * A_up B + bias_up[r])
+   The gated form is the SwiGLU of an MLP (A = W_gate, A_up = W_up, act = SiLU,
+   silu(x) = x / (1 + e^-x)): one launch streams both weights against one
+   staged B and writes one output.  A_up has A's shape, dtype and row rules;
+   its metadata must be a tcgen05 image (SP24_META_TC) and so must d->meta in
+   the gated form.  The gated form runs on the narrow-N kernel (tiles up to
+   128 columns; any N). */
+typedef enum sp24_activation {
+  SP24_ACT_NONE = 0,
+  SP24_ACT_SILU = 1
+} sp24_activation;
+
+typedef struct sp24_epilogue {
+  const float* bias;          /* optional, m floats (device) */
+  sp24_activation act;
+  const void* a_c_up;         /* gated form when not NULL: compressed A_up, m x k/2 */
+  int64_t lda_c_up;           /* elements; 0 = k/2 */
+  const uint8_t* meta_up;     /* A_up's tcgen05 metadata image */
+  float alpha_up;             /* 0 = 1.0 */
+  const float* bias_up;       /* optional, m floats */
+} sp24_epilogue;
+
+/* sp24_gemm followed by the epilogue `e` (NULL = none), in one launch. */
+sp24_status sp24_gemm_fused(const sp24_gemm_desc* d, const sp24_epilogue* e,
+                            sp24_stream_t stream);
+
 /* FP8 helpers.
    sp24_amax_f32: amax_dev[0] = max |x| over count floats (device).
    sp24_quantize_e4m3: q[i] = e4m3_rn_satfinite(x[i] * scale[0]) with

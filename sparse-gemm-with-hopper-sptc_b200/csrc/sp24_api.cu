@@ -146,6 +146,13 @@ struct Prepared {
   int64_t ldc;
   float alpha;
   uint32_t idesc_ab;
+  const float* bias;
+  int act;
+  const void* a_c_up;  // gated form (split-K kernel only)
+  int64_t lda_c_up;
+  const uint8_t* meta_up;
+  float alpha_up;
+  const float* bias_up;
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -192,6 +199,8 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.ldc = p.ldc;
   P.alpha = p.alpha;
   P.idesc_ab = p.idesc_ab;
+  P.bias = p.bias;
+  P.act = p.act;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -258,6 +267,8 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   P.ldc = p.ldc;
   P.alpha = p.alpha;
   P.idesc_ab = p.idesc_ab;
+  P.bias = p.bias;
+  P.act = p.act;
   P.vec_f32 = p.c_f32 == nullptr                            ? 0
               : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
               : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
@@ -330,10 +341,10 @@ int choose_splits(Kern kern, int smem, int tiles, int stages, int sm_count) {
   return s;
 }
 
-template <int DT, int BN, int KB>
+template <int DT, int BN, int KB, int G>
 sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
-  using C = sp24::SplitCfg<DT, BN, KB>;
-  auto kern = sp24::sp24_gemm_splitk_kernel<DT, BN, KB>;
+  using C = sp24::SplitCfg<DT, BN, KB, G>;
+  auto kern = sp24::sp24_gemm_splitk_kernel<DT, BN, KB, G>;
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   SP24_CUDA_TRY(cudaGetDevice(&dev));
@@ -354,6 +365,13 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
                  static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::UK,
                  swizzle_for_span(C::B_SPAN));
   if (st != SP24_OK) return st;
+  CUtensorMap ta2 = ta;
+  if constexpr (G == 2) {
+    st = encode_2d(&ta2, tdt, p.a_c_up, static_cast<uint64_t>(p.k / 2),
+                   static_cast<uint64_t>(p.m), static_cast<uint64_t>(p.lda_c_up) * C::ESZ,
+                   C::A_COLS, sp24::kBlockM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != SP24_OK) return st;
+  }
 
   sp24::SplitParams P{};
   P.m = p.m;
@@ -370,11 +388,16 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.ldc = p.ldc;
   P.alpha = p.alpha;
   P.idesc_ab = p.idesc_ab;
+  P.bias = p.bias;
+  P.act = p.act;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
+  P.meta_up = p.meta_up;
+  P.alpha_up = p.alpha_up;
+  P.bias_up = p.bias_up;
   const int tiles = P.m_blocks * P.n_tiles;
   P.splits = choose_splits(kern, C::SMEM_BYTES, tiles, P.stages, di.sm_count);
 
@@ -390,7 +413,7 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SP24_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, P));
+  SP24_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, ta2, P));
   return SP24_OK;
 }
 
@@ -441,10 +464,22 @@ using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_
 template <int DT>
 LaunchFn pick_splitk(int bn, int kb) {
   switch (bn) {
-    case 16: return kb == 2 ? launch_splitk<DT, 16, 2> : launch_splitk<DT, 16, 1>;
-    case 32: return kb == 2 ? launch_splitk<DT, 32, 2> : launch_splitk<DT, 32, 1>;
-    case 64: return kb == 2 ? launch_splitk<DT, 64, 2> : launch_splitk<DT, 64, 1>;
-    default: return kb == 2 ? launch_splitk<DT, 128, 2> : launch_splitk<DT, 128, 1>;
+    case 16: return kb == 2 ? launch_splitk<DT, 16, 2, 1> : launch_splitk<DT, 16, 1, 1>;
+    case 32: return kb == 2 ? launch_splitk<DT, 32, 2, 1> : launch_splitk<DT, 32, 1, 1>;
+    case 64: return kb == 2 ? launch_splitk<DT, 64, 2, 1> : launch_splitk<DT, 64, 1, 1>;
+    default: return kb == 2 ? launch_splitk<DT, 128, 2, 1> : launch_splitk<DT, 128, 1, 1>;
+  }
+}
+
+// Gated form: two weights per ring slot, so one unit per stage keeps four to
+// five slots in flight.
+template <int DT>
+LaunchFn pick_gated(int bn) {
+  switch (bn) {
+    case 16: return launch_splitk<DT, 16, 1, 2>;
+    case 32: return launch_splitk<DT, 32, 1, 2>;
+    case 64: return launch_splitk<DT, 64, 1, 2>;
+    default: return launch_splitk<DT, 128, 1, 2>;
   }
 }
 
@@ -527,9 +562,24 @@ sp24_status validate(const sp24_gemm_desc* d) {
   return SP24_OK;
 }
 
+// Checks of the epilogue descriptor (after the GEMM descriptor passed validate).
+sp24_status validate_epilogue(const sp24_gemm_desc* d, const sp24_epilogue* e) {
+  if (e == nullptr) return SP24_OK;
+  if (e->act != SP24_ACT_NONE && e->act != SP24_ACT_SILU) return SP24_ERR_ARG;
+  if (e->a_c_up == nullptr) return SP24_OK;
+  if (e->meta_up == nullptr || d->meta_format != SP24_META_TC) return SP24_ERR_ARG;
+  const int64_t lda = e->lda_c_up ? e->lda_c_up : d->k / 2;
+  if (lda < d->k / 2) return SP24_ERR_SHAPE;
+  if (!aligned16(e->a_c_up) || ((lda * esize(d->dtype)) % 16) != 0 || !aligned16(e->meta_up))
+    return SP24_ERR_ALIGN;
+  return SP24_OK;
+}
+
 sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned long long timeout_ns,
-                      int stall) {
+                      int stall, const sp24_epilogue* e = nullptr) {
   sp24_status st = validate(d);
+  if (st != SP24_OK) return st;
+  st = validate_epilogue(d, e);
   if (st != SP24_OK) return st;
   const WsPlan w = plan_workspace(d);
   if (w.total > 0 && (d->workspace == nullptr || d->workspace_bytes < w.total))
@@ -554,6 +604,15 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   p.ldc = d->ldc ? d->ldc : d->n;
   p.alpha = d->alpha == 0.0f ? 1.0f : d->alpha;
   p.idesc_ab = idesc_ab(d->dtype);
+  if (e != nullptr) {
+    p.bias = e->bias;
+    p.act = e->act == SP24_ACT_SILU ? sp24::kActSilu : sp24::kActNone;
+    p.a_c_up = e->a_c_up;
+    p.lda_c_up = e->lda_c_up ? e->lda_c_up : d->k / 2;
+    p.meta_up = e->meta_up;
+    p.alpha_up = e->alpha_up == 0.0f ? 1.0f : e->alpha_up;
+    p.bias_up = e->bias_up;
+  }
   p.status = d->status_dev ? d->status_dev : di->status_word;
   p.timeout_ns = timeout_ns;
   p.stall_producer = stall;
@@ -577,6 +636,13 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     p.ldb = w.b_pitch_elems;
   }
 
+  if (p.a_c_up != nullptr) {
+    const int bn = std::min(128, choose_bn(d->m, d->n, d->tile_n, di->sm_count));
+    LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)
+                  : d->dtype == SP24_BF16 ? pick_gated<1>(bn)
+                                          : pick_gated<2>(bn);
+    return gf(p, *di, stream);
+  }
   if (use_pair_kernel(d->m, d->n, d->tile_n)) {
     const bool fine = pair_fine_stages();
     LaunchFn pf = d->dtype == SP24_F16    ? (fine ? launch_gemm2sm<0, 1> : launch_gemm2sm<0, 0>)
@@ -675,6 +741,11 @@ sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream) {
 
 // Allocation-free sp24_gemm: the scratch sp24_gemm would take from
 // d->workspace comes from the fixed device buffer g_sp24_noalloc_scratch.
+sp24_status sp24_gemm_fused(const sp24_gemm_desc* d, const sp24_epilogue* e,
+                            sp24_stream_t stream) {
+  return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0, e);
+}
+
 sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream) {
   sp24_status st = validate(d);
   if (st != SP24_OK) return st;

@@ -54,6 +54,8 @@ struct PairParams {
   uint32_t idesc_ab;  // A / B format fields of the instruction descriptor for mixed fp8
                       // (A at bit 7, B at bit 10; e5m2 = 1), 0 otherwise
   float alpha;
+  const float* bias;  // optional per-row bias (m floats)
+  int act;            // kActNone / kActSilu
   int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
   int vec_bf16;
   int* status;
@@ -124,7 +126,17 @@ SP24_DEV void st_global_v8_u32(void* p, const uint32_t* v) {
 // Store 128 consecutive accumulator columns of one row (already in registers).
 SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, int col0) {
   if (row >= P.m) return;
-  const float alpha = P.alpha;
+  // The epilogue is applied in place, so the stores below see final values.
+  if (P.bias != nullptr || P.act != kActNone) {
+    const bool hb = P.bias != nullptr;
+    const float b = hb ? P.bias[row] : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 128; ++i)
+      r[i] = __float_as_uint(epi_value(__uint_as_float(r[i]), P.alpha, b, hb, P.act));
+  } else if (P.alpha != 1.0f) {
+#pragma unroll
+    for (int i = 0; i < 128; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * P.alpha);
+  }
   const bool full = col0 + 128 <= P.n;
   if (P.c_f32 != nullptr) {
     float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col0;
@@ -133,19 +145,19 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
       for (int i = 0; i < 128; i += 8) {
         float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]) * alpha;
+        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]);
         st_global_v8(dst + i, v);
       }
     } else if (full && P.vec_f32 == 1) {
 #pragma unroll
       for (int i = 0; i < 128; i += 4)
         *reinterpret_cast<float4*>(dst + i) =
-            make_float4(__uint_as_float(r[i]) * alpha, __uint_as_float(r[i + 1]) * alpha,
-                        __uint_as_float(r[i + 2]) * alpha, __uint_as_float(r[i + 3]) * alpha);
+            make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
+                        __uint_as_float(r[i + 3]));
     } else {
 #pragma unroll
       for (int i = 0; i < 128; ++i)
-        if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]) * alpha;
+        if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]);
     }
   }
   if (P.c_bf16 != nullptr) {
@@ -156,8 +168,8 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
         uint32_t pk[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[i + 2 * j]) * alpha,
-                                                   __uint_as_float(r[i + 2 * j + 1]) * alpha);
+          __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[i + 2 * j]),
+                                                   __uint_as_float(r[i + 2 * j + 1]));
           pk[j] = *reinterpret_cast<uint32_t*>(&h);
         }
         if (P.vec_bf16 == 2) {
@@ -170,7 +182,7 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
     } else {
 #pragma unroll
       for (int i = 0; i < 128; ++i)
-        if (col0 + i < P.n) dst[i] = __float2bfloat16_rn(__uint_as_float(r[i]) * alpha);
+        if (col0 + i < P.n) dst[i] = __float2bfloat16_rn(__uint_as_float(r[i]));
     }
   }
 }

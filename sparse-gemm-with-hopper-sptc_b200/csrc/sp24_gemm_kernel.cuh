@@ -41,6 +41,20 @@ constexpr int kThreads = 192;          // 6 warps
 constexpr int kAtomBytes = 2048;       // 128 lanes x 16 B metadata atom
 constexpr int kSmemBudget = 232448 - 2048;
 
+// Output epilogue shared by every kernel: per row r,
+//   v = alpha * acc (+ bias[r]), then the activation (none or SiLU).
+// The bias is a per-row vector because A holds the weights (output features
+// along M) and B the activations (tokens along N).
+enum : int { kActNone = 0, kActSilu = 1 };
+
+SP24_DEV float silu(float v) { return v / (1.0f + __expf(-v)); }
+
+SP24_DEV float epi_value(float acc, float alpha, float bias, bool has_bias, int act) {
+  float v = acc * alpha;
+  if (has_bias) v += bias;
+  return act == kActSilu ? silu(v) : v;
+}
+
 struct GemmParams {
   int m, n, k;
   int m_blocks, n_tiles, k_stages, num_tiles;
@@ -53,6 +67,8 @@ struct GemmParams {
   uint32_t idesc_ab;  // A / B format fields of the instruction descriptor for mixed fp8
                       // (A at bit 7, B at bit 10; e5m2 = 1), 0 otherwise
   float alpha;
+  const float* bias;  // optional per-row bias (m floats), added after alpha
+  int act;            // kActNone / kActSilu, applied last
   int vec_f32;   // 16-byte vector stores allowed for c_f32
   int vec_bf16;  // 16-byte vector stores allowed for c_bf16
   int* status;   // device word: set to 1 when a bounded wait timed out
@@ -118,14 +134,11 @@ SP24_DEV void tile_coords(const GemmParams& P, int t, int& mb, int& nb) {
   nb = r / gm;
 }
 
-// PP: any parameter block with m, n, ldc, alpha, c_f32, c_bf16, vec_f32, vec_bf16.
+// Stores N finished values of one row.  PP: any parameter block with m, n,
+// ldc, c_f32, c_bf16, vec_f32, vec_bf16.
 template <int N, typename PP>
-SP24_DEV void store_chunk(const PP& P, uint32_t (&r)[N], int row, int col) {
+SP24_DEV void store_values(const PP& P, const float (&v)[N], int row, int col) {
   if (row >= P.m) return;
-  const float alpha = P.alpha;
-  float v[N];
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]) * alpha;
   const bool full = (col + N <= P.n);
   if (P.c_f32 != nullptr) {
     float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col;
@@ -161,6 +174,19 @@ SP24_DEV void store_chunk(const PP& P, uint32_t (&r)[N], int row, int col) {
         if (col + i < P.n) dst[i] = __float2bfloat16_rn(v[i]);
     }
   }
+}
+
+// N accumulator columns of one row -> epilogue -> stores.  PP additionally
+// carries alpha, bias and act.
+template <int N, typename PP>
+SP24_DEV void store_chunk(const PP& P, uint32_t (&r)[N], int row, int col) {
+  if (row >= P.m) return;
+  const bool hb = P.bias != nullptr;
+  const float b = hb ? P.bias[row] : 0.0f;
+  float v[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = epi_value(__uint_as_float(r[i]), P.alpha, b, hb, P.act);
+  store_values<N>(P, v, row, col);
 }
 
 template <int DT, int BN>

@@ -22,6 +22,11 @@
 //     partials over DSMEM in rank order (a fixed order: results do not depend
 //     on timing) and stores them.  No workspace, no atomics, no second launch.
 //
+// Gated form (G = 2, the SwiGLU of an MLP): the CTA streams W_gate and W_up
+// (same shape, same B) through one ring, accumulates both tiles in TMEM and
+// writes act(alpha W_gate B + bias) * (alpha_up W_up B + bias_up) once.  B is
+// staged once for both, and the two GEMMs share one launch and one output.
+//
 // Roles (6 warps, as in sp24_gemm_kernel.cuh): warp 0 TMA producer, warp 1
 // TMEM owner and MMA issuer, warps 2..5 epilogue (TMEM lane quarters).
 //
@@ -53,6 +58,12 @@ struct SplitParams {
   uint32_t idesc_ab;  // A / B format fields of the instruction descriptor for mixed fp8
                       // (A at bit 7, B at bit 10; e5m2 = 1), 0 otherwise
   float alpha;
+  const float* bias;  // optional per-row bias (m floats)
+  int act;            // kActNone / kActSilu
+  // Gated form only: the second weight's metadata image, scale and bias.
+  const uint8_t* meta_up;
+  float alpha_up;
+  const float* bias_up;
   int vec_f32;
   int vec_bf16;
   int* status;
@@ -60,10 +71,12 @@ struct SplitParams {
   int stall_producer;
 };
 
-template <int DT, int BN, int KB>
+// G: weights streamed per CTA (1 plain, 2 gated).
+template <int DT, int BN, int KB, int G = 1>
 struct SplitCfg {
   static constexpr int ESZ = (DT == 2) ? 1 : 2;
   static constexpr int KIND = (DT == 2) ? 1 : 0;
+  static constexpr int WEIGHTS = G;
   static constexpr int UK = (DT == 2) ? 256 : 128;        // dense K per unit
   static constexpr int MMA_K = (DT == 2) ? 64 : 32;
   static constexpr int MMAS_U = UK / MMA_K;               // 4
@@ -71,7 +84,7 @@ struct SplitCfg {
   static constexpr int BKD = KB * UK;                     // dense K per stage
   static constexpr int A_COLS = 128 / ESZ;                // compressed values per A box row
   static constexpr int A_BOX = kBlockM * 128;             // 16 KB
-  static constexpr int A_BYTES = KB * A_BOX;
+  static constexpr int A_BYTES = G * KB * A_BOX;           // gate units, then up units
   static constexpr int B_ROW = BN * ESZ;
   static constexpr int B_SPAN = B_ROW >= 128 ? 128 : B_ROW;
   static constexpr int B_BOXN = B_SPAN / ESZ;
@@ -85,17 +98,18 @@ struct SplitCfg {
   static constexpr uint32_t B_LBO = B_LAYOUT == kLayoutNone ? 8 * B_SPAN : B_BOX_BYTES;
   static constexpr uint32_t B_SBO = B_LAYOUT == kLayoutNone ? B_BOX_BYTES : 8 * B_SPAN;
   static constexpr int B_MMA_ADVANCE = MMA_K * B_SPAN;
-  static constexpr int E_S = KB * E_U;                    // metadata atoms per stage
-  static constexpr int E_BYTES = E_S * kAtomBytes;
+  static constexpr int E_S = KB * E_U;                    // metadata atoms per stage and weight
+  static constexpr int E_BYTES = G * E_S * kAtomBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
   static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-  static constexpr int LOADS_A = KB;
+  static constexpr int LOADS_A = G * KB;
   static constexpr int LOADS_B = KB * B_BOXES;
-  static constexpr int LOADS = LOADS_A + LOADS_B + E_S;   // one copy per producer lane
+  static constexpr int LOADS = LOADS_A + LOADS_B + G * E_S;   // one copy per producer lane
   static constexpr uint32_t LOAD_LANES = LOADS == 32 ? 0xffffffffu : (1u << LOADS) - 1u;
-  static constexpr int COLS_NEEDED = BN + 2 * E_S * 4;
+  static constexpr int E_COL = G * BN;                    // accumulators first, then metadata
+  static constexpr int COLS_NEEDED = E_COL + 2 * G * E_S * 4;
   static constexpr uint32_t TMEM_COLS = COLS_NEEDED <= 32    ? 32
                                         : COLS_NEEDED <= 64  ? 64
                                         : COLS_NEEDED <= 128 ? 128
@@ -111,7 +125,7 @@ struct SplitCfg {
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(LOADS <= 32, "one producer lane per copy");
-  static_assert(kBlockM * RS * 4 <= STAGES * STAGE_BYTES, "partial tile must fit the ring");
+  static_assert(G * kBlockM * RS * 4 <= STAGES * STAGE_BYTES, "partial tiles must fit the ring");
 };
 
 // Bytes that land on a slot's full barrier for global stage g: every A and B
@@ -122,17 +136,13 @@ SP24_DEV uint32_t split_stage_tx(const SplitParams& P, int g) {
   const int a0 = g * C::E_S;
   int atoms = P.katoms - a0;
   atoms = atoms < 0 ? 0 : (atoms > C::E_S ? C::E_S : atoms);
-  return static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + atoms * kAtomBytes);
+  return static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + C::WEIGHTS * atoms * kAtomBytes);
 }
 
+// Stores four finished values of one row.
 template <typename PP>
 SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
   if (row >= P.m) return;
-  const float alpha = P.alpha;
-  v.x *= alpha;
-  v.y *= alpha;
-  v.z *= alpha;
-  v.w *= alpha;
   const bool full = col + 4 <= P.n;
   if (P.c_f32 != nullptr) {
     float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col;
@@ -165,12 +175,28 @@ SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
 
 // Grid: (m_blocks * n_tiles * S) CTAs in clusters of S along x; CTA rank r of
 // cluster t computes tile t over stages [stages*r/S, stages*(r+1)/S).
-template <int DT, int BN, int KB>
+// Epilogue of one output element from its fp32 sums: the plain form applies
+// alpha, bias and the activation; the gated form multiplies the activated
+// gate by the up projection.
+template <int G>
+SP24_DEV float split_out(const SplitParams& P, float g, float u, float bg, float bu) {
+  const float a = epi_value(g, P.alpha, bg, P.bias != nullptr, P.act);
+  if constexpr (G == 1) {
+    (void)u, (void)bu;
+    return a;
+  } else {
+    return a * epi_value(u, P.alpha_up, bu, P.bias_up != nullptr, kActNone);
+  }
+}
+
+// tmA2: W_up's A_c (gated form; the plain form passes tmA again).
+template <int DT, int BN, int KB, int G>
 __global__ void __launch_bounds__(kThreads, 1)
     sp24_gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmA,
-                            const __grid_constant__ CUtensorMap tmB, const SplitParams P) {
+                            const __grid_constant__ CUtensorMap tmB,
+                            const __grid_constant__ CUtensorMap tmA2, const SplitParams P) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using C = SplitCfg<DT, BN, KB>;
+  using C = SplitCfg<DT, BN, KB, G>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -209,6 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (G == 2) tma_prefetch_desc(&tmA2);
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
@@ -222,15 +249,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Lane l issues copy l of every stage: A boxes, then B boxes, then
-    // metadata atoms.  Coordinates advance by a constant step per stage.
+    // Lane l issues copy l of every stage: A boxes (gate units, then up
+    // units), then B boxes, then metadata atoms (gate, then up).
+    // Coordinates advance by a constant step per stage.
     if (!P.stall_producer && lane < C::LOADS) {
       const bool is_a = lane < C::LOADS_A;
       const bool is_b = !is_a && lane < C::LOADS_A + C::LOADS_B;
       const int bl = lane - C::LOADS_A;
       const int el = lane - C::LOADS_A - C::LOADS_B;
-      const int u = is_a ? lane : (is_b ? bl / C::B_BOXES : 0);
-      const uint32_t off = is_a   ? static_cast<uint32_t>(u * C::A_BOX)
+      const int u = is_a ? lane % KB : (is_b ? bl / C::B_BOXES : 0);
+      const bool up = is_a ? (lane >= KB) : (!is_b && el >= C::E_S);
+      const CUtensorMap* amap = up ? &tmA2 : &tmA;
+      const uint8_t* meta = up ? P.meta_up : P.meta_tc;
+      const uint32_t off = is_a   ? static_cast<uint32_t>(lane * C::A_BOX)
                            : is_b ? static_cast<uint32_t>(C::A_BYTES + u * C::B_UNIT +
                                                           (bl % C::B_BOXES) * C::B_BOX_BYTES)
                                   : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + el * kAtomBytes);
@@ -239,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int y = is_a ? mb * kBlockM : (is_b ? (g0 * KB + u) * C::UK : 0);
       const int dx = is_a ? KB * C::A_COLS : 0;
       const int dy = is_b ? C::BKD : 0;
-      int atom = g0 * C::E_S + el;
+      int atom = g0 * C::E_S + (up ? el - C::E_S : el);
       int s = 0;
       uint32_t ph = 0, soff = 0;
       uint32_t issued_mask = 0, issued_ph = 0;
@@ -253,11 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* dst = smem + soff + off;
         if (is_a) {
-          tma_load_2d(dst, &tmA, &full_bar[s], x, y);
+          tma_load_2d(dst, amap, &full_bar[s], x, y);
         } else if (is_b) {
           tma_load_2d(dst, &tmB, &full_bar[s], x, y);
         } else if (atom < P.katoms) {
-          bulk_load(dst, P.meta_tc + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
+          bulk_load(dst, meta + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
                     kAtomBytes, &full_bar[s]);
         }
         if (lane == 0) {
@@ -297,30 +328,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && i + C::STAGES < nst)
         mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, g + C::STAGES));
       tc_fence_after();
-      ebuf ^= static_cast<uint32_t>(C::E_S * 4);
-      const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(BN) + ebuf;
+      ebuf ^= static_cast<uint32_t>(G * C::E_S * 4);
+      const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
 #pragma unroll
-      for (int a = 0; a < C::E_S; ++a)
-        if (g * C::E_S + a < P.katoms)
+      for (int a = 0; a < G * C::E_S; ++a)
+        if (g * C::E_S + a % C::E_S < P.katoms)
           tc_cp_elect<1>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
       const int kleft = P.k - g * C::BKD;
 #pragma unroll
-      for (int u = 0; u < KB; ++u)
+      for (int w = 0; w < G; ++w)
 #pragma unroll
-        for (int j = 0; j < C::MMAS_U; ++j) {
-          const int kk = u * C::UK + j * C::MMA_K;   // dense K inside the stage
-          if (kk < kleft) {
-            const int atom_in = kk / 128;
-            const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>((kk % 128) / 32)
-                                                : static_cast<uint32_t>(2 * ((kk % 128) / 64));
-            const uint64_t ad = adesc0 + soff + u * (C::A_BOX >> 4) + j * 2;
-            const uint64_t bd =
-                bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4);
-            tc_mma_sp_elect<1, C::KIND>(tmem_base, ad, bd, e_tmem + 4 * atom_in + (col & ~1u),
-                                        C::IDESC | P.idesc_ab | (col & 1u),
-                                        (i > 0 || kk > 0) ? 1u : 0u);
+        for (int u = 0; u < KB; ++u)
+#pragma unroll
+          for (int j = 0; j < C::MMAS_U; ++j) {
+            const int kk = u * C::UK + j * C::MMA_K;   // dense K inside the stage
+            if (kk < kleft) {
+              const int atom_in = w * C::E_S + kk / 128;
+              const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>((kk % 128) / 32)
+                                                  : static_cast<uint32_t>(2 * ((kk % 128) / 64));
+              const uint64_t ad = adesc0 + soff + (w * KB + u) * (C::A_BOX >> 4) + j * 2;
+              const uint64_t bd =
+                  bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4);
+              tc_mma_sp_elect<1, C::KIND>(tmem_base + static_cast<uint32_t>(w * BN), ad, bd,
+                                          e_tmem + 4 * atom_in + (col & ~1u),
+                                          C::IDESC | P.idesc_ab | (col & 1u),
+                                          (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
-        }
       any = true;
       tc_commit_elect<1>(&empty_bar[s], 0);
       soff += SD;
@@ -342,25 +376,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       tc_fence_after();
       const int row_l = q * 32 + lane;
+      const int row = mb * kBlockM + row_l;
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
       float* red = reinterpret_cast<float*>(smem);   // ring is idle once accf has fired
+      const bool live = row < P.m;
+      const float bg = (P.bias != nullptr && live) ? P.bias[row] : 0.0f;
+      const float bu = (G == 2 && P.bias_up != nullptr && live) ? P.bias_up[row] : 0.0f;
 #pragma unroll 1
       for (int c = 0; c < BN; c += C::CH) {
-        uint32_t r[C::CH];
-        if constexpr (C::CH == 32) {
-          tmem_ld_x32(tb + c, r);
-        } else {
-          tmem_ld_x16(tb + c, r);
+        uint32_t r[G][C::CH];
+#pragma unroll
+        for (int w = 0; w < G; ++w) {
+          if constexpr (C::CH == 32) {
+            tmem_ld_x32(tb + static_cast<uint32_t>(w * BN + c), r[w]);
+          } else {
+            tmem_ld_x16(tb + static_cast<uint32_t>(w * BN + c), r[w]);
+          }
         }
-        tmem_ld_wait(r);
+#pragma unroll
+        for (int w = 0; w < G; ++w) tmem_ld_wait(r[w]);
         if (S == 1) {
-          store_chunk<C::CH>(P, r, mb * kBlockM + row_l, nb * BN + c);
+          float v[C::CH];
+#pragma unroll
+          for (int e = 0; e < C::CH; ++e)
+            v[e] = split_out<G>(P, __uint_as_float(r[0][e]), __uint_as_float(r[G - 1][e]), bg,
+                                bu);
+          store_values<C::CH>(P, v, row, nb * BN + c);
         } else {
 #pragma unroll
-          for (int v = 0; v < C::CH; v += 4)
-            *reinterpret_cast<float4*>(red + row_l * C::RS + c + v) =
-                make_float4(__uint_as_float(r[v]), __uint_as_float(r[v + 1]),
-                            __uint_as_float(r[v + 2]), __uint_as_float(r[v + 3]));
+          for (int w = 0; w < G; ++w)
+#pragma unroll
+            for (int v = 0; v < C::CH; v += 4)
+              *reinterpret_cast<float4*>(red + (w * kBlockM + row_l) * C::RS + c + v) =
+                  make_float4(__uint_as_float(r[w][v]), __uint_as_float(r[w][v + 1]),
+                              __uint_as_float(r[w][v + 2]), __uint_as_float(r[w][v + 3]));
         }
       }
     }
@@ -379,16 +428,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int idx = threadIdx.x; idx < (r1 - r0) * NV; idx += kThreads) {
       const int rl = r0 + idx / NV;
       const int cg = idx - (idx / NV) * NV;
-      const uint32_t la = smem_u32(red + rl * C::RS + cg * 4);
-      float4 acc = ld_dsmem_f4(mapa_shared(la, 0));
-      for (int src = 1; src < S; ++src) {
-        const float4 v = ld_dsmem_f4(mapa_shared(la, static_cast<uint32_t>(src)));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+      const int row = mb * kBlockM + rl;
+      float4 acc[G];
+#pragma unroll
+      for (int w = 0; w < G; ++w) {
+        const uint32_t la = smem_u32(red + (w * kBlockM + rl) * C::RS + cg * 4);
+        acc[w] = ld_dsmem_f4(mapa_shared(la, 0));
+        for (int src = 1; src < S; ++src) {
+          const float4 v = ld_dsmem_f4(mapa_shared(la, static_cast<uint32_t>(src)));
+          acc[w].x += v.x;
+          acc[w].y += v.y;
+          acc[w].z += v.z;
+          acc[w].w += v.w;
+        }
       }
-      store_vec4(P, acc, mb * kBlockM + rl, nb * BN + cg * 4);
+      if (row >= P.m) continue;
+      const float bg = P.bias != nullptr ? P.bias[row] : 0.0f;
+      const float bu = (G == 2 && P.bias_up != nullptr) ? P.bias_up[row] : 0.0f;
+      const float4 o = make_float4(split_out<G>(P, acc[0].x, acc[G - 1].x, bg, bu),
+                                   split_out<G>(P, acc[0].y, acc[G - 1].y, bg, bu),
+                                   split_out<G>(P, acc[0].z, acc[G - 1].z, bg, bu),
+                                   split_out<G>(P, acc[0].w, acc[G - 1].w, bg, bu));
+      store_vec4(P, o, row, nb * BN + cg * 4);
     }
     // No CTA leaves (and releases its shared memory) while others still read it.
     cluster_sync();

@@ -37,8 +37,10 @@ EXPORTS = [
     "sp24_gemm_workspace_bytes", "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta",
     "sp24_gemm", "sp24_last_kernel_status", "sp24_selftest_timeout", "sp24_amax_f32",
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
-    "sp24_gemm_noalloc", "sp24_quantize_e5m2",
+    "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused",
 ]
+
+ACT_NONE, ACT_SILU = 0, 1
 
 
 class Sp24Error(RuntimeError):
@@ -57,6 +59,14 @@ class GemmDesc(Structure):
         ("alpha", c_float), ("tile_n", c_int),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("status_dev", c_void_p),
+    ]
+
+
+class Epilogue(Structure):
+    _fields_ = [
+        ("bias", c_void_p), ("act", c_int),
+        ("a_c_up", c_void_p), ("lda_c_up", c_int64), ("meta_up", c_void_p),
+        ("alpha_up", c_float), ("bias_up", c_void_p),
     ]
 
 
@@ -81,6 +91,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_gemm_workspace_bytes.argtypes = [POINTER(GemmDesc)]
     lib.sp24_gemm.argtypes = [POINTER(GemmDesc), c_void_p]
     lib.sp24_gemm_noalloc.argtypes = [POINTER(GemmDesc), c_void_p]
+    lib.sp24_gemm_fused.argtypes = [POINTER(GemmDesc), POINTER(Epilogue), c_void_p]
     lib.sp24_selftest_timeout.argtypes = [POINTER(GemmDesc), c_ulonglong, c_void_p]
     lib.sp24_last_kernel_status.argtypes = [c_void_p]
     lib.sp24_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
@@ -98,7 +109,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                        POINTER(c_int)]
     lib.sp24_unshard_columns_f32.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                              c_void_p]
-    for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_selftest_timeout", "sp24_last_kernel_status",
+    for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_gemm_fused", "sp24_selftest_timeout",
+                 "sp24_last_kernel_status",
                  "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_amax_f32",
                  "sp24_quantize_e4m3", "sp24_quantize_e5m2", "sp24_unshard_columns_f32",
                  "sp24_check_device"):
@@ -228,6 +240,34 @@ def gemm(a_c, meta, b, m, n, k, *, meta_format=META_REF, out_f32=True, out_bf16=
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
         d.workspace, d.workspace_bytes = workspace.data_ptr(), need
     _check(lib.sp24_gemm(ctypes.byref(d), _stream(stream)), "sp24_gemm")
+    return c_f32, c_bf16
+
+
+def gemm_fused(a_c, meta, b, m, n, k, *, bias=None, act=ACT_NONE, a_c_up=None, meta_up=None,
+               alpha_up=1.0, bias_up=None, meta_format=META_TC, out_f32=True, out_bf16=False,
+               alpha=1.0, tile_n=0, c_f32=None, c_bf16=None, stream=None, dtype=None):
+    """sp24_gemm_fused: C = act(alpha A B + bias) [* (alpha_up A_up B + bias_up)]."""
+    import torch
+    lib = load()
+    dev = a_c.device
+    if out_f32 and c_f32 is None:
+        c_f32 = torch.empty((m, n), dtype=torch.float32, device=dev)
+    if out_bf16 and c_bf16 is None:
+        c_bf16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    d = make_desc(a_c, meta, b, m, n, k, meta_format=meta_format, c_f32=c_f32, c_bf16=c_bf16,
+                  alpha=alpha, tile_n=tile_n, dtype=dtype)
+    need = workspace_bytes(d)
+    ws = None
+    if need:
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        d.workspace, d.workspace_bytes = ws.data_ptr(), need
+    e = Epilogue()
+    e.bias, e.act = _ptr(bias), act
+    e.a_c_up = _ptr(a_c_up)
+    e.lda_c_up = 0 if a_c_up is None else a_c_up.stride(0)
+    e.meta_up, e.alpha_up, e.bias_up = _ptr(meta_up), alpha_up, _ptr(bias_up)
+    _check(lib.sp24_gemm_fused(ctypes.byref(d), ctypes.byref(e), _stream(stream)),
+           "sp24_gemm_fused")
     return c_f32, c_bf16
 
 

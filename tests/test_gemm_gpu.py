@@ -411,6 +411,91 @@ def test_e5m2_quantize_and_prune_match_oracle():
     np.testing.assert_array_equal(pruned.cpu().numpy(), oracle.prune_2of4(oracle.E5M2, q_ref))
 
 
+# ------------------------------------------------------------------ fused epilogues
+def _silu(x):
+    return x / (1.0 + np.exp(-x.astype(np.float64)))
+
+
+@pytest.mark.parametrize("kernel,m,n,k,splits", [("2sm", 512, 512, 512, ""), ("1sm", 256, 192, 256, ""),
+                                                 ("splitk", 384, 40, 2048, "1"),
+                                                 ("splitk", 256, 16, 4096, "4")])
+@pytest.mark.parametrize("act", [sp24.ACT_NONE, sp24.ACT_SILU])
+def test_bias_and_silu_epilogue(kernel, m, n, k, splits, act):
+    """C = act(alpha A B + bias[row]) on every kernel: against the oracle's
+    GEMM with the epilogue applied on the host (row-norm bound), and against
+    the library's own plain GEMM with the epilogue applied afterwards in fp32."""
+    gen = oracle.Gen(m + n + act)
+    a, b, _, _, c_ref = oracle.host_case(gen, 1, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, 1))
+    img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
+    b_t = to_dev(b, 1)
+    bias = torch.from_numpy(np.random.default_rng(m).uniform(-2, 2, m).astype(np.float32)).to(DEV)
+    alpha = 0.75
+    env = {"SP24_KERNEL": kernel, **({"SP24_SPLITS": splits} if splits else {})}
+
+    def run():
+        fused, _ = sp24.gemm_fused(ac_t, img, b_t, m, n, k, bias=bias, act=act, alpha=alpha)
+        plain, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC)
+        return fused, plain
+
+    fused, plain = _with_env(env, run)
+    torch.cuda.synchronize()
+    pre = plain.double() * alpha + bias.double()[:, None]
+    want = pre if act == sp24.ACT_NONE else pre / (1 + torch.exp(-pre))
+    assert ((fused.double() - want).abs() / (want.abs() + 1)).max().item() < 1e-5
+    pre_ref = c_ref.astype(np.float64) * alpha + bias.cpu().numpy()[:, None]
+    ref = pre_ref if act == sp24.ACT_NONE else _silu(pre_ref)
+    err = oracle.row_norm_rel_error(fused.cpu().numpy(), ref.astype(np.float32),
+                                    oracle.to_float(1, a) * alpha, oracle.to_float(1, b))
+    assert err <= 1e-2, err
+
+
+@pytest.mark.parametrize("m,n,k,splits", [(256, 16, 4096, ""), (4096, 8, 2048, "4"),
+                                          (300, 100, 1024, "3"), (256, 256, 512, "")])
+@pytest.mark.parametrize("dt", [1, 2])
+def test_gated_silu_mlp(m, n, k, splits, dt):
+    """SwiGLU in one launch: silu(alpha W_gate B + b_g) * (alpha_up W_up B + b_u)
+    against the same composition of two plain GEMMs (fp32 on the host), and
+    against the oracle's fp32 GEMMs with a bound scaled by both factors."""
+    gen = oracle.Gen(m * 3 + n + dt)
+    wg, b, _, _, g_ref = oracle.host_case(gen, dt, m, n, k, False)
+    wu, _, _, _, _ = oracle.host_case(gen, dt, m, n, k, False)
+    u_ref = oracle.gemm(dt, wu, b)
+    ld = lib_dtype(dt)
+    acg, eg = sp24.compress(to_dev(wg, dt))
+    acu, eu = sp24.compress(to_dev(wu, dt))
+    img_g, img_u = sp24.repack_meta(eg, m, k, ld), sp24.repack_meta(eu, m, k, ld)
+    b_t = to_dev(b, dt)
+    rng = np.random.default_rng(n)
+    bg = torch.from_numpy(rng.uniform(-1, 1, m).astype(np.float32)).to(DEV)
+    bu = torch.from_numpy(rng.uniform(-1, 1, m).astype(np.float32)).to(DEV)
+    env = {"SP24_SPLITS": splits} if splits else {}
+
+    def run():
+        out, out16 = sp24.gemm_fused(acg, img_g, b_t, m, n, k, bias=bg, act=sp24.ACT_SILU,
+                                     a_c_up=acu, meta_up=img_u, alpha=0.5, alpha_up=2.0,
+                                     bias_up=bu, out_bf16=True, dtype=ld)
+        g, _ = sp24.gemm(acg, img_g, b_t, m, n, k, meta_format=sp24.META_TC, dtype=ld)
+        u, _ = sp24.gemm(acu, img_u, b_t, m, n, k, meta_format=sp24.META_TC, dtype=ld)
+        return out, out16, g, u
+
+    out, out16, g, u = _with_env(env, run) if env else run()
+    torch.cuda.synchronize()
+    assert torch.equal(out16, out.to(torch.bfloat16))
+    gp = g.double() * 0.5 + bg.double()[:, None]
+    up = u.double() * 2.0 + bu.double()[:, None]
+    want = gp / (1 + torch.exp(-gp)) * up
+    scale = (gp.abs() + 1) * (up.abs() + 1)
+    assert ((out.double() - want).abs() / scale).max().item() < 1e-5
+    gr = g_ref.astype(np.float64) * 0.5 + bg.cpu().numpy()[:, None]
+    ur = u_ref.astype(np.float64) * 2.0 + bu.cpu().numpy()[:, None]
+    ref = _silu(gr) * ur
+    af, bf = oracle.to_float(dt, wg), oracle.to_float(dt, b)
+    rowscale = np.outer(np.linalg.norm(af, axis=1), np.linalg.norm(bf, axis=0)) / np.sqrt(k)
+    bound = rowscale * (2.0 * (np.abs(ur) + 1) + 0.5 * (np.abs(_silu(gr)) + 1))
+    assert (np.abs(out.cpu().numpy() - ref) / bound).max() <= TOL[dt]
+
+
 # ------------------------------------------------------------------ full-size properties
 def test_config2_bf16_8192_sampled_rows():
     """Benchmark configuration 2 at full size (bf16 8192^3, U(-1,1), uniform
