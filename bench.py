@@ -72,6 +72,12 @@ def config_for(args):
         cfg["n"] = args.tokens
         cfg["name"] = cfg["name"].format(layer="W_up/W_gate" if up else "W_down", m=cfg["m"],
                                          k=cfg["k"], n=cfg["n"])
+        if args.gated:
+            if not up:
+                raise SystemExit("--gated applies to the W_up/W_gate layer")
+            cfg["name"] = (f"bf16 MLP SwiGLU silu(W_gate B) * (W_up B), W 14336x4096 x T={cfg['n']},"
+                           " one fused launch, magnitude-pruned N(0,0.02) (config 4)")
+            cfg["gemms"] = 2
     return cfg
 
 
@@ -154,11 +160,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(cfg, rank, torch, sp24):
+def make_inputs(cfg, rank, torch, sp24, seed_a=1234):
     """Device-resident A (2:4), its compression + tcgen05 metadata image, B."""
     dev = torch.device("cuda")
     dt, m, n, k = cfg["dt"], cfg["m"], cfg["n"], cfg["k"]
-    g = torch.Generator(device=dev).manual_seed(1234)          # A replicated on every rank
+    g = torch.Generator(device=dev).manual_seed(seed_a)        # A replicated on every rank
     gb = torch.Generator(device=dev).manual_seed(4321 + rank)  # B: this rank's column block
     tdt = {0: torch.float16, 1: torch.bfloat16, 2: torch.float8_e4m3fn}[dt]
     scale_a = scale_b = 1.0
@@ -289,6 +295,9 @@ def main():
                     help="configuration 4: activation columns T (8, 16, 64, 128 or 4096)")
     ap.add_argument("--layer", default="up", choices=["up", "down"],
                     help="configuration 4: W_up/W_gate (14336x4096) or W_down (4096x14336)")
+    ap.add_argument("--gated", action="store_true",
+                    help="configuration 4, W_up/W_gate: one fused SwiGLU launch "
+                         "(silu(W_gate B) * W_up B) per step instead of one GEMM")
     ap.add_argument("--steps-ref", type=int, default=1)
     ap.add_argument("--warmup-ref", type=int, default=1)
     args = ap.parse_args()
@@ -325,8 +334,21 @@ def main():
     sptr = stream.cuda_stream
     lib = sp24.load()
 
+    gemms = cfg.get("gemms", 1)
+    if gemms == 2:
+        # Second weight (W_up) of the SwiGLU; W_gate is `ac`.
+        cfg_up = dict(cfg)
+        ac_up, _, img_up, _, _ = make_inputs(cfg_up, rank, torch, sp24, seed_a=4242)
+        epi = sp24.Epilogue()
+        epi.act = sp24.ACT_SILU
+        epi.a_c_up, epi.lda_c_up = ac_up.data_ptr(), ac_up.stride(0)
+        epi.meta_up, epi.alpha_up = img_up.data_ptr(), 1.0
+
     def step():
-        rc = lib.sp24_gemm(ctypes.byref(desc), sptr)
+        if gemms == 2:
+            rc = lib.sp24_gemm_fused(ctypes.byref(desc), ctypes.byref(epi), sptr)
+        else:
+            rc = lib.sp24_gemm(ctypes.byref(desc), sptr)
         if rc != 0:
             raise sp24.Sp24Error(rc, "sp24_gemm")
 
@@ -341,7 +363,7 @@ def main():
     # and each step is timed alone with its own events.
     esz = 1 if dt == 2 else 2
     out_bytes = sum(4 if o == "f32" else 2 for o in cfg["out"]) * m * n
-    in_bytes = m * k // 2 * esz + m * k // 8 + k * n * esz
+    in_bytes = gemms * (m * k // 2 * esz + m * k // 8) + k * n * esz
     flush_l2 = in_bytes + out_bytes < 2 * L2_BYTES
     if flush_l2:
         flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
@@ -385,9 +407,43 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total = t.item()
     ms_step = ms_total / args.steps
-    flops_rank = 2.0 * m * n * k
+    flops_rank = 2.0 * m * n * k * gemms
     value = flops_rank * world / (ms_step * 1e-3) / 1e12
     kernel_tflops = flops_rank / (ms_local / args.steps * 1e-3) / 1e12
+
+    # Gated mode: the same SwiGLU as two GEMMs plus torch's silu * mul, timed
+    # the same way, for comparison.
+    unfused = None
+    if gemms == 2:
+        g16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        u16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        dg = sp24.make_desc(ac, img, b, m, n, k, meta_format=sp24.META_TC, c_bf16=g16,
+                            dtype=lib_dt)
+        du = sp24.make_desc(ac_up, img_up, b, m, n, k, meta_format=sp24.META_TC, c_bf16=u16,
+                            dtype=lib_dt)
+
+        def unfused_step():
+            lib.sp24_gemm(ctypes.byref(dg), sptr)
+            lib.sp24_gemm(ctypes.byref(du), sptr)
+            torch.mul(torch.nn.functional.silu(g16), u16, out=c16)
+
+        for _ in range(3):
+            unfused_step()
+        torch.cuda.synchronize()
+        uevs = []
+        for _ in range(min(args.steps, 50)):
+            if flush_l2:
+                clean_l2()
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            unfused_step()
+            a1.record(stream)
+            uevs.append((a0, a1))
+        torch.cuda.synchronize()
+        ums = sum(x.elapsed_time(y) for x, y in uevs) / len(uevs)
+        unfused = {"ms_per_step": ums, "launches_per_step": 2 + 2,
+                   "what": "two sp24_gemm calls (bf16 out) + torch silu(g) * u"}
 
     # Optional replicated output: all-gather of the C shards over NVLink,
     # timed separately from the GEMM (config 5 option).
@@ -423,7 +479,41 @@ def main():
 
     # End to end through the public C ABI with host buffers.
     e2e = None
-    if args.e2e_steps > 0:
+    if args.e2e_steps > 0 and gemms == 2:
+        # Gated: both weights travel with their tcgen05 images (the fused form
+        # takes pre-packed metadata), then one fused launch, then C.
+        hs = [x.cpu().pin_memory() for x in (ac, img, ac_up, img_up, b)]
+        ds = [torch.empty_like(x) for x in (ac, img, ac_up, img_up, b)]
+        h_c16 = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+        d2 = sp24.make_desc(ds[0], ds[1], ds[4], m, n, k, meta_format=sp24.META_TC, c_bf16=c16,
+                            alpha=alpha, dtype=lib_dt)
+        epi2 = sp24.Epilogue()
+        epi2.act, epi2.a_c_up, epi2.lda_c_up = sp24.ACT_SILU, ds[2].data_ptr(), ds[2].stride(0)
+        epi2.meta_up, epi2.alpha_up = ds[3].data_ptr(), 1.0
+
+        def e2e_step():
+            for d_x, h_x in zip(ds, hs):
+                d_x.copy_(h_x, non_blocking=True)
+            rc = lib.sp24_gemm_fused(ctypes.byref(d2), ctypes.byref(epi2), sptr)
+            if rc != 0:
+                raise sp24.Sp24Error(rc, "sp24_gemm_fused")
+            h_c16.copy_(c16, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        x0 = torch.cuda.Event(enable_timing=True)
+        x1 = torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        x1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = x0.elapsed_time(x1) / args.e2e_steps
+        e2e = {"value": flops_rank * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in hs),
+               "d2h_bytes_per_step": h_c16.numel() * 2, "ms_per_step": ms_e2e,
+               "steps": args.e2e_steps, "gpu_launches_per_step": 1}
+    elif args.e2e_steps > 0:
         h_ac = ac.cpu().pin_memory()
         h_meta = meta.cpu().pin_memory()
         h_b = b.cpu().pin_memory()
@@ -481,7 +571,8 @@ def main():
         ms_kernel = ms_local / args.steps
         hbm_bound = args.config == 4 and n <= 128
         tag = {2: "sp24_gemm2sm_bf16_8192", 3: "sp24_gemm2sm_e4m3_16384",
-               4: f"sp24_gemm_mlp_{args.layer}_T{n}", 5: "sp24_gemm2sm_f16_32768"}[args.config]
+               4: f"sp24_gemm_mlp_{args.layer}_T{n}" + ("_gated" if gemms == 2 else ""),
+               5: "sp24_gemm2sm_f16_32768"}[args.config]
         if hbm_bound:
             gbps = alg_bytes / (ms_kernel * 1e-3) / 1e9
             roofline = {"bound": "hbm", "achieved": gbps, "peak": hbm_peak, "unit": "GB/s",
@@ -519,6 +610,8 @@ def main():
         }
         if allgather:
             line["allgather"] = allgather
+        if unfused:
+            line["unfused_comparison"] = unfused
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -153,6 +153,7 @@ struct Prepared {
   const uint8_t* meta_up;
   float alpha_up;
   const float* bias_up;
+  int gate_from_c;
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -201,6 +202,7 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.idesc_ab = p.idesc_ab;
   P.bias = p.bias;
   P.act = p.act;
+  P.gate_from_c = p.gate_from_c;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -269,6 +271,7 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   P.idesc_ab = p.idesc_ab;
   P.bias = p.bias;
   P.act = p.act;
+  P.gate_from_c = p.gate_from_c;
   P.vec_f32 = p.c_f32 == nullptr                            ? 0
               : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
               : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
@@ -390,6 +393,7 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.idesc_ab = p.idesc_ab;
   P.bias = p.bias;
   P.act = p.act;
+  P.gate_from_c = p.gate_from_c;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -562,6 +566,9 @@ sp24_status validate(const sp24_gemm_desc* d) {
   return SP24_OK;
 }
 
+sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const DeviceInfo& di,
+                         cudaStream_t stream);
+
 // Checks of the epilogue descriptor (after the GEMM descriptor passed validate).
 sp24_status validate_epilogue(const sp24_gemm_desc* d, const sp24_epilogue* e) {
   if (e == nullptr) return SP24_OK;
@@ -638,11 +645,41 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
 
   if (p.a_c_up != nullptr) {
     const int bn = std::min(128, choose_bn(d->m, d->n, d->tile_n, di->sm_count));
-    LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)
-                  : d->dtype == SP24_BF16 ? pick_gated<1>(bn)
-                                          : pick_gated<2>(bn);
-    return gf(p, *di, stream);
+    const long long tiles = static_cast<long long>((d->m + 127) / 128) * ((d->n + bn - 1) / bn);
+    if (d->n <= 128 || tiles <= 4LL * di->sm_count) {
+      // One launch: both weights through the split-K kernel's ring.
+      LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)
+                    : d->dtype == SP24_BF16 ? pick_gated<1>(bn)
+                                            : pick_gated<2>(bn);
+      return gf(p, *di, stream);
+    }
+    // Wide N (compute-bound): two passes on the regular kernels with C as the
+    // intermediate.  Pass 1 writes act(alpha W_gate B + bias) into C (fp32
+    // when the caller asked for it, else bf16); pass 2 multiplies
+    // (alpha_up W_up B + bias_up) by it in its epilogue and writes the result.
+    Prepared p1 = p;
+    p1.a_c_up = nullptr;
+    if (p1.c_f32 != nullptr) p1.c_bf16 = nullptr;
+    st = launch_plain(d, p1, *di, stream);
+    if (st != SP24_OK) return st;
+    Prepared p2 = p;
+    p2.a_c_up = nullptr;
+    p2.a_c = p.a_c_up;
+    p2.lda_c = p.lda_c_up;
+    p2.meta_tc = p.meta_up;
+    p2.alpha = p.alpha_up;
+    p2.bias = p.bias_up;
+    p2.act = sp24::kActNone;
+    p2.gate_from_c = 1;
+    return launch_plain(d, p2, *di, stream);
   }
+  return launch_plain(d, p, *di, stream);
+}
+
+// The kernel choice for one plain (or pass-of-two) GEMM.
+sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const DeviceInfo& di_ref,
+                         cudaStream_t stream) {
+  const DeviceInfo* di = &di_ref;
   if (use_pair_kernel(d->m, d->n, d->tile_n)) {
     const bool fine = pair_fine_stages();
     LaunchFn pf = d->dtype == SP24_F16    ? (fine ? launch_gemm2sm<0, 1> : launch_gemm2sm<0, 0>)

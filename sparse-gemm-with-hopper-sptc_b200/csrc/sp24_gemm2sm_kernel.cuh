@@ -56,6 +56,8 @@ struct PairParams {
   float alpha;
   const float* bias;  // optional per-row bias (m floats)
   int act;            // kActNone / kActSilu
+  int gate_from_c;    // second pass of a two-pass gated epilogue: multiply by the value
+                      // already in C (c_f32 if given, else c_bf16) before storing
   int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
   int vec_bf16;
   int* status;
@@ -137,6 +139,7 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
 #pragma unroll
     for (int i = 0; i < 128; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * P.alpha);
   }
+  if (P.gate_from_c) gate_mul_row<128>(P, reinterpret_cast<float*>(r), row, col0);
   const bool full = col0 + 128 <= P.n;
   if (P.c_f32 != nullptr) {
     float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col0;

@@ -69,6 +69,8 @@ struct GemmParams {
   float alpha;
   const float* bias;  // optional per-row bias (m floats), added after alpha
   int act;            // kActNone / kActSilu, applied last
+  int gate_from_c;    // second pass of a two-pass gated epilogue: multiply by the value
+                      // already in C (c_f32 if given, else c_bf16) before storing
   int vec_f32;   // 16-byte vector stores allowed for c_f32
   int vec_bf16;  // 16-byte vector stores allowed for c_bf16
   int* status;   // device word: set to 1 when a bounded wait timed out
@@ -176,8 +178,46 @@ SP24_DEV void store_values(const PP& P, const float (&v)[N], int row, int col) {
   }
 }
 
+// Value already in C at (row, col) (f32 output if present, else bf16).
+template <typename PP>
+SP24_DEV float load_c(const PP& P, int row, int col) {
+  const long long o = static_cast<long long>(row) * P.ldc + col;
+  return P.c_f32 != nullptr ? P.c_f32[o] : __bfloat162float(P.c_bf16[o]);
+}
+
+// v[i] *= C[row][col + i] for the N columns of one row segment (the second
+// pass of a two-pass gated epilogue).  16-byte loads when the segment is
+// whole and C's rows allow them; the same thread stores the segment later.
+template <int N, typename PP>
+SP24_DEV void gate_mul_row(const PP& P, float* v, int row, int col) {
+  const long long o = static_cast<long long>(row) * P.ldc + col;
+  const bool full = col + N <= P.n;
+  if (full && P.c_f32 != nullptr && P.vec_f32) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 g = *reinterpret_cast<const float4*>(P.c_f32 + o + i);
+      v[i] *= g.x, v[i + 1] *= g.y, v[i + 2] *= g.z, v[i + 3] *= g.w;
+    }
+  } else if (full && P.c_f32 == nullptr && P.vec_bf16 && N % 8 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 8) {
+      const uint4 pk = *reinterpret_cast<const uint4*>(P.c_bf16 + o + i);
+      const uint32_t w[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[i + 2 * j] *= __uint_as_float(w[j] << 16);
+        v[i + 2 * j + 1] *= __uint_as_float(w[j] & 0xFFFF0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (col + i < P.n) v[i] *= load_c(P, row, col + i);
+  }
+}
+
 // N accumulator columns of one row -> epilogue -> stores.  PP additionally
-// carries alpha, bias and act.
+// carries alpha, bias, act and gate_from_c.
 template <int N, typename PP>
 SP24_DEV void store_chunk(const PP& P, uint32_t (&r)[N], int row, int col) {
   if (row >= P.m) return;
@@ -186,6 +226,7 @@ SP24_DEV void store_chunk(const PP& P, uint32_t (&r)[N], int row, int col) {
   float v[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = epi_value(__uint_as_float(r[i]), P.alpha, b, hb, P.act);
+  if (P.gate_from_c) gate_mul_row<N>(P, v, row, col);
   store_values<N>(P, v, row, col);
 }
 

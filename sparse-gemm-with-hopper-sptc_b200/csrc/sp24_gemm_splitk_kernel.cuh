@@ -60,6 +60,8 @@ struct SplitParams {
   float alpha;
   const float* bias;  // optional per-row bias (m floats)
   int act;            // kActNone / kActSilu
+  int gate_from_c;    // second pass of a two-pass gated epilogue: multiply by the value
+                      // already in C (c_f32 if given, else c_bf16) before storing
   // Gated form only: the second weight's metadata image, scale and bias.
   const uint8_t* meta_up;
   float alpha_up;
@@ -401,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < C::CH; ++e)
             v[e] = split_out<G>(P, __uint_as_float(r[0][e]), __uint_as_float(r[G - 1][e]), bg,
                                 bu);
+          if (P.gate_from_c && live) gate_mul_row<C::CH>(P, v, row, nb * BN + c);
           store_values<C::CH>(P, v, row, nb * BN + c);
         } else {
 #pragma unroll
@@ -445,11 +448,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (row >= P.m) continue;
       const float bg = P.bias != nullptr ? P.bias[row] : 0.0f;
       const float bu = (G == 2 && P.bias_up != nullptr) ? P.bias_up[row] : 0.0f;
-      const float4 o = make_float4(split_out<G>(P, acc[0].x, acc[G - 1].x, bg, bu),
-                                   split_out<G>(P, acc[0].y, acc[G - 1].y, bg, bu),
-                                   split_out<G>(P, acc[0].z, acc[G - 1].z, bg, bu),
-                                   split_out<G>(P, acc[0].w, acc[G - 1].w, bg, bu));
-      store_vec4(P, o, row, nb * BN + cg * 4);
+      float4 o = make_float4(split_out<G>(P, acc[0].x, acc[G - 1].x, bg, bu),
+                             split_out<G>(P, acc[0].y, acc[G - 1].y, bg, bu),
+                             split_out<G>(P, acc[0].z, acc[G - 1].z, bg, bu),
+                             split_out<G>(P, acc[0].w, acc[G - 1].w, bg, bu));
+      const int col = nb * BN + cg * 4;
+      if (P.gate_from_c) {
+        if (col + 0 < P.n) o.x *= load_c(P, row, col + 0);
+        if (col + 1 < P.n) o.y *= load_c(P, row, col + 1);
+        if (col + 2 < P.n) o.z *= load_c(P, row, col + 2);
+        if (col + 3 < P.n) o.w *= load_c(P, row, col + 3);
+      }
+      store_vec4(P, o, row, col);
     }
     // No CTA leaves (and releases its shared memory) while others still read it.
     cluster_sync();

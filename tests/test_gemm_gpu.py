@@ -496,6 +496,51 @@ def test_gated_silu_mlp(m, n, k, splits, dt):
     assert (np.abs(out.cpu().numpy() - ref) / bound).max() <= TOL[dt]
 
 
+@pytest.mark.parametrize("outs", ["f32", "bf16", "both"])
+def test_gated_two_pass_for_wide_n(outs):
+    """Wide N (more than four waves of 128-wide tiles): the gated form runs as
+    two passes on the regular kernels, the second multiplying by the first's
+    result held in C.  Checked against the composition of two plain GEMMs
+    (fp32 intermediate; a bf16-only output keeps the intermediate in bf16)
+    and, on sampled rows, against the oracle."""
+    m, n, k, dt = 2048, 8192, 256, 1
+    gen = oracle.Gen(99)
+    wg, b, _, _, _ = oracle.host_case(gen, dt, m, 8, k, False)
+    wu, _, _, _, _ = oracle.host_case(gen, dt, m, 8, k, False)
+    b = oracle.from_float(dt, np.random.default_rng(5).uniform(-1, 1, (k, n)).astype(np.float32))
+    acg, eg = sp24.compress(to_dev(wg, dt))
+    acu, eu = sp24.compress(to_dev(wu, dt))
+    img_g = sp24.repack_meta(eg, m, k, torch.bfloat16)
+    img_u = sp24.repack_meta(eu, m, k, torch.bfloat16)
+    b_t = to_dev(b, dt)
+    out, out16 = sp24.gemm_fused(acg, img_g, b_t, m, n, k, act=sp24.ACT_SILU, a_c_up=acu,
+                                 meta_up=img_u, alpha_up=1.5, out_f32=outs != "bf16",
+                                 out_bf16=outs != "f32")
+    g, _ = sp24.gemm(acg, img_g, b_t, m, n, k, meta_format=sp24.META_TC)
+    u, _ = sp24.gemm(acu, img_u, b_t, m, n, k, meta_format=sp24.META_TC)
+    torch.cuda.synchronize()
+    sg = torch.nn.functional.silu(g)
+    if outs == "bf16":
+        want = sg.to(torch.bfloat16).float() * (1.5 * u)
+        got = out16.float()
+        tol = 2 ** -7
+    else:
+        want = sg * (1.5 * u)
+        got = out
+        tol = 1e-5
+        if outs == "both":
+            assert torch.equal(out16, out.to(torch.bfloat16))
+    assert ((got - want).abs() / (want.abs() + 1)).max().item() < tol
+    rows = np.sort(np.random.default_rng(1).choice(m, 16, replace=False))
+    gr = oracle.gemm(dt, wg[rows], b).astype(np.float64)
+    ur = oracle.gemm(dt, wu[rows], b).astype(np.float64) * 1.5
+    ref = _silu(gr) * ur
+    af, bf = oracle.to_float(dt, wg[rows]), oracle.to_float(dt, b)
+    rowscale = np.outer(np.linalg.norm(af, axis=1), np.linalg.norm(bf, axis=0)) / np.sqrt(k)
+    bound = rowscale * (1.5 * (np.abs(ur) + 1) + np.abs(_silu(gr)) + 1)
+    assert (np.abs(got[rows].cpu().numpy() - ref) / bound).max() <= 1e-2
+
+
 # ------------------------------------------------------------------ full-size properties
 def test_config2_bf16_8192_sampled_rows():
     """Benchmark configuration 2 at full size (bf16 8192^3, U(-1,1), uniform
