@@ -76,7 +76,16 @@ typedef enum sp24_meta_format {
      (wgmma_sp_raw_common.hpp:197-202).  Needs workspace (repacked on the fly). */
   SP24_META_REF = 0,
   /* The tcgen05 image written by sp24_repack_meta (sp24_meta_tc_bytes bytes). */
-  SP24_META_TC = 1
+  SP24_META_TC = 1,
+  /* The m16n8k16 layout of the reference's legacy warp-level entry points
+     (mma_sp_m16n8k16_fp32{fp16,bf16}.cu:96-110, strips concatenated at :277-297):
+     u32 words [K/16][M/2]; word (s, 8b+i) holds row 16b+i's four nibbles of the
+     16-wide K strip s in bits 0-15 and row 16b+8+i's in bits 16-31.  fp16/bf16
+     only, M % 16 == 0.  Needs workspace (repacked on the fly).
+     (The m16n8k32 entry points' metadata, u32 words [M][K/32] with group g of a
+     word at bits 4g..4g+3 (mma_sp_m16n8k32_fp32fp16.cu:112-118), is the
+     SP24_META_REF byte stream read little-endian: pass it as SP24_META_REF.) */
+  SP24_META_K16 = 2
 } sp24_meta_format;
 
 /* Output selection bits for sp24_gemm_desc.c_f32 / c_bf16: either may be NULL,
@@ -133,6 +142,10 @@ sp24_status sp24_prune_2of4(sp24_dtype dtype, const void* a, int m, int k, int64
    sp24_gemm with SP24_META_TC.  Padding groups get the valid code 0x4. */
 sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, int k,
                              uint8_t* meta_tc, sp24_stream_t stream);
+
+/* The same image from metadata in the m16n8k16 layout (SP24_META_K16). */
+sp24_status sp24_repack_meta_k16(sp24_dtype dtype, const uint32_t* meta_k16, int m, int k,
+                                 uint8_t* meta_tc, sp24_stream_t stream);
 
 /* The GEMM.  Reference: wgmma_sp_raw_kernel<Element,BlockN>
    (wgmma_sp_raw_common.hpp:955-1030), grid (N/BlockN, M/64) x 128 threads,

@@ -77,6 +77,8 @@ def lib():
         o.oracle_quantize_e5m2.restype = c_float
         o.oracle_quantize_e5m2.argtypes = [c_void_p, c_size_t, c_void_p]
         o.oracle_to_float.argtypes = [c_int, c_void_p, c_size_t, c_void_p]
+        o.oracle_gen_legacy.argtypes = [c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]
+        o.oracle_meta_k16_from_ref.argtypes = [c_void_p, c_int, c_int, c_void_p]
         o.oracle_from_float.argtypes = [c_int, c_void_p, c_size_t, c_void_p]
         _o = o
     return _o
@@ -101,6 +103,54 @@ def ref_lib():
         r.ref_cpu_gemm.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int]
         _r = r
     return _r
+
+
+REF_LEGACY_LIB = os.path.join(HERE, "_ref", "libsp24ref_legacy.so")
+# The reference's legacy warp-level entry points, as ref_legacy_case numbers them.
+LEGACY_FILES = ["mma_sp_m16n8k16_fp32fp16.cu", "mma_sp_m16n8k16_fp32bf16.cu",
+                "mma_sp_m16n8k32_fp32fp16.cu", "mma_sp_m16n8k32_fp32bf16.cu"]
+
+
+def legacy_dtype(which: int) -> int:
+    return F16 if which in (0, 2) else BF16
+
+
+def gen_legacy(which: int, m: int, n: int, k: int):
+    """(A dense, B) of the legacy main `which` (mt19937(42), that main's order)."""
+    dt = legacy_dtype(which)
+    a = np.empty((m, k), np.uint16)
+    b = np.empty((k, n), np.uint16)
+    lib().oracle_gen_legacy(0 if which < 2 else 1, dt, m, n, k, _p(a), _p(b))
+    return a, b
+
+
+def meta_k16_from_ref(meta, m: int, k: int):
+    """Reference-layout metadata bytes -> m16n8k16 words [k/16][m/2] (uint32)."""
+    out = np.empty((k // 16, m // 2), np.uint32)
+    lib().oracle_meta_k16_from_ref(_p(np.ascontiguousarray(meta)), m, k, _p(out))
+    return out
+
+
+def ref_legacy_available() -> bool:
+    return os.path.exists(REF_LEGACY_LIB)
+
+
+def ref_legacy_case(which: int, m: int, n: int, k: int, with_c: bool = True):
+    """A legacy main replayed by the reference's own host code at m x n x k:
+    (a, b, a_c, meta words, c or None); meta is [k/16][m/2] words for the
+    m16n8k16 mains and [m][k/32] for the m16n8k32 ones."""
+    r = ctypes.CDLL(REF_LEGACY_LIB)
+    r.ref_legacy_case.restype = c_int
+    r.ref_legacy_case.argtypes = [c_int, c_int, c_int, c_int] + [c_void_p] * 5
+    a = np.empty((m, k), np.uint16)
+    b = np.empty((k, n), np.uint16)
+    ac = np.empty((m, k // 2), np.uint16)
+    e = np.empty((k // 16, m // 2) if which < 2 else (m, k // 32), np.uint32)
+    c = np.empty((m, n), np.float32) if with_c else None
+    rc = r.ref_legacy_case(which, m, n, k, _p(a), _p(b), _p(ac), _p(e),
+                           _p(c) if with_c else None)
+    assert rc == 0
+    return a, b, ac, e, c
 
 
 def ref_fp8_available() -> bool:

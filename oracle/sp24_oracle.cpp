@@ -150,6 +150,47 @@ void oracle_gen_pattern_b(int dt, int k, int n, void* b_out) {
     }
 }
 
+// The legacy warp-level entry points' generation (mma_sp_m16n8k16_fp32fp16.cu /
+// mma_sp_m16n8k32_fp32fp16.cu and their bf16 twins), mt19937(42):
+//   A: per row, per group of four, two distinct positions (second redrawn until
+//      it differs, then ordered) and two U(-1,1) values, 0 replaced by +1 / -1
+//      (init_structured_sparse_A, :29-56);
+//   order (which = 0, m16n8k16 mains, :265-268): A, then B[i] = U(-1,1);
+//   order (which = 1, m16n8k32 mains, :426-437): A[i] = U(-1,1) and
+//      B[i] = U(-1,1) for every element, then A overwritten as above.
+void oracle_gen_legacy(int which, int dt, int m, int n, int k, void* a_out, void* b_out) {
+  std::mt19937 gen(42);
+  std::uniform_real_distribution<float> uni(-1.0f, 1.0f);
+  auto structured = [&]() {
+    std::uniform_real_distribution<float> dist(-1.0f, 1.0f);
+    std::uniform_int_distribution<int> pos(0, 3);
+    const uint32_t zero = from_f(dt, 0.0f);
+    for (size_t i = 0; i < static_cast<size_t>(m) * k; ++i) st(dt, a_out, i, zero);
+    for (int r = 0; r < m; ++r)
+      for (int grp = 0; grp < k / 4; ++grp) {
+        int p = pos(gen);
+        int q = pos(gen);
+        while (q == p) q = pos(gen);
+        const int lo = std::min(p, q), hi = std::max(p, q);
+        float x = dist(gen);
+        float y = dist(gen);
+        if (x == 0.0f) x = 1.0f;
+        if (y == 0.0f) y = -1.0f;
+        const size_t base = static_cast<size_t>(r) * k + grp * 4;
+        st(dt, a_out, base + lo, from_f(dt, x));
+        st(dt, a_out, base + hi, from_f(dt, y));
+      }
+  };
+  if (which == 0) {
+    structured();
+    for (size_t i = 0; i < static_cast<size_t>(k) * n; ++i) st(dt, b_out, i, from_f(dt, uni(gen)));
+  } else {
+    for (size_t i = 0; i < static_cast<size_t>(m) * k; ++i) st(dt, a_out, i, from_f(dt, uni(gen)));
+    for (size_t i = 0; i < static_cast<size_t>(k) * n; ++i) st(dt, b_out, i, from_f(dt, uni(gen)));
+    structured();
+  }
+}
+
 // ---------------------------------------------------------------- compress
 // Returns -1 when every group holds exactly two nonzeros, else the first bad
 // group as row*(k/4)+group (the reference prints it and exits).
@@ -304,6 +345,22 @@ void oracle_meta_tc_image(int dt, const uint8_t* meta, int m, int k, uint32_t* i
           }
           img[((static_cast<size_t>(ka) * mb_n + mb) * 128 + L) * 4 + w] = word;
         }
+}
+
+// Reference-layout metadata -> the m16n8k16 layout of the legacy entry points
+// (mma_sp_m16n8k16_fp32fp16.cu:96-110, strips concatenated at :277-297): word
+// (s, 8b+i) = row 16b+i's 16-bit strip s (bytes 2s, 2s+1 of its metadata row)
+// | row 16b+8+i's << 16.  m % 16 == 0, k % 16 == 0.
+void oracle_meta_k16_from_ref(const uint8_t* meta, int m, int k, uint32_t* out) {
+  const int rb = k / 8;
+  for (int strip = 0; strip < k / 16; ++strip)
+    for (int blk = 0; blk < m / 16; ++blk)
+      for (int i = 0; i < 8; ++i) {
+        const uint8_t* lo = meta + static_cast<size_t>(16 * blk + i) * rb + 2 * strip;
+        const uint8_t* hi = meta + static_cast<size_t>(16 * blk + 8 + i) * rb + 2 * strip;
+        out[static_cast<size_t>(strip) * (m / 2) + 8 * blk + i] =
+            (lo[0] | (lo[1] << 8)) | (static_cast<uint32_t>(hi[0] | (hi[1] << 8)) << 16);
+      }
 }
 
 // Per-tensor fp8 quantisation: scale = largest finite value / amax (448 for

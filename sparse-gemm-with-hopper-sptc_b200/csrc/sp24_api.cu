@@ -531,7 +531,7 @@ bool b_needs_copy(const sp24_gemm_desc* d) {
 WsPlan plan_workspace(const sp24_gemm_desc* d) {
   WsPlan w;
   size_t off = 0;
-  if (d->meta_format == SP24_META_REF) {
+  if (d->meta_format == SP24_META_REF || d->meta_format == SP24_META_K16) {
     w.meta_off = off;
     w.meta_bytes = sp24_meta_tc_bytes(d->m, d->k);
     off = round_up(off + w.meta_bytes, 256);
@@ -550,7 +550,11 @@ WsPlan plan_workspace(const sp24_gemm_desc* d) {
 sp24_status validate(const sp24_gemm_desc* d) {
   if (d == nullptr) return SP24_ERR_ARG;
   if (!dtype_ok(d->dtype)) return SP24_ERR_ARG;
-  if (d->meta_format != SP24_META_REF && d->meta_format != SP24_META_TC) return SP24_ERR_ARG;
+  if (d->meta_format != SP24_META_REF && d->meta_format != SP24_META_TC &&
+      d->meta_format != SP24_META_K16)
+    return SP24_ERR_ARG;
+  if (d->meta_format == SP24_META_K16 && (is_fp8(d->dtype) || d->m % 16 != 0))
+    return SP24_ERR_SHAPE;
   if (d->m <= 0 || d->n <= 0 || d->k <= 0) return SP24_ERR_SHAPE;
   const int kq = is_fp8(d->dtype) ? 64 : 32;
   if (d->k % kq != 0) return SP24_ERR_SHAPE;
@@ -627,6 +631,11 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   if (d->meta_format == SP24_META_REF) {
     st = sp24_repack_meta(d->dtype, d->meta, d->m, d->k, ws + w.meta_off,
                           reinterpret_cast<sp24_stream_t>(stream));
+    if (st != SP24_OK) return st;
+    p.meta_tc = ws + w.meta_off;
+  } else if (d->meta_format == SP24_META_K16) {
+    st = sp24_repack_meta_k16(d->dtype, reinterpret_cast<const uint32_t*>(d->meta), d->m, d->k,
+                              ws + w.meta_off, reinterpret_cast<sp24_stream_t>(stream));
     if (st != SP24_OK) return st;
     p.meta_tc = ws + w.meta_off;
   } else {
@@ -902,6 +911,24 @@ sp24_status sp24_repack_meta(sp24_dtype dtype, const uint8_t* meta_ref, int m, i
   cudaStream_t s = as_stream(stream);
   sp24::repack_meta_kernel<<<grid_for(total, 256), 256, 0, s>>>(
       meta_ref, m, k, is_fp8(dtype) ? 1 : 0, reinterpret_cast<uint32_t*>(meta_tc), mb, ka);
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+sp24_status sp24_repack_meta_k16(sp24_dtype dtype, const uint32_t* meta_k16, int m, int k,
+                                 uint8_t* meta_tc, sp24_stream_t stream) {
+  if (!dtype_ok(dtype) || is_fp8(dtype) || meta_k16 == nullptr || meta_tc == nullptr)
+    return SP24_ERR_ARG;
+  if (m <= 0 || k <= 0 || k % 32 != 0 || m % 16 != 0) return SP24_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(meta_tc) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(meta_k16) & 3u) != 0)
+    return SP24_ERR_ALIGN;
+  const int mb = meta_mblocks(m);
+  const int ka = meta_katoms(k);
+  const long long total = static_cast<long long>(ka) * mb * 128 * 4;
+  cudaStream_t s = as_stream(stream);
+  sp24::repack_meta_kernel<<<grid_for(total, 256), 256, 0, s>>>(
+      nullptr, m, k, 0, reinterpret_cast<uint32_t*>(meta_tc), mb, ka, meta_k16);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
 }

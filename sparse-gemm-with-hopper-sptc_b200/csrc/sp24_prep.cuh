@@ -149,8 +149,15 @@ __global__ void prune_kernel(const uint8_t* __restrict__ a, int m, int k, long l
 //  e4m3 (kind::f8f6f4, two columns per K=64 MMA):
 //    lane L = row L; the 16 bytes are the row's 16 reference bytes of the atom.
 // Groups outside [0,m) x [0,k) get the valid code 0x4 (indices 0,1).
+// k16 != nullptr: the source is the reference's m16n8k16 layout instead
+// (16-bit types, m % 16 == 0): u32 words [k/16 strips][m/2], word (s, 8b+i)
+// holding row 16b+i's four nibbles of strip s in bits 0-15 and row 16b+8+i's
+// in bits 16-31 (mma_sp_m16n8k16_fp32fp16.cu:96-110, strips concatenated at
+// :277-297).  That pairing of rows r and r+8 per 16-row block is exactly the
+// lane pairing of the 16-bit TMEM image, so each image word is one k16 word.
 __global__ void repack_meta_kernel(const uint8_t* __restrict__ ref, int m, int k, int is8,
-                                   uint32_t* __restrict__ img, int m_blocks, int k_atoms) {
+                                   uint32_t* __restrict__ img, int m_blocks, int k_atoms,
+                                   const uint32_t* __restrict__ k16 = nullptr) {
   const long long total = static_cast<long long>(k_atoms) * m_blocks * 128 * 4;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;
@@ -170,6 +177,13 @@ __global__ void repack_meta_kernel(const uint8_t* __restrict__ ref, int m, int k
     } else {
       word = 0x44444444u;
     }
+  } else if (k16 != nullptr) {
+    const int m2 = L >> 4, k1 = (L >> 3) & 1, m0 = L & 7;
+    const int kr = ka * 128 + 32 * w + 16 * k1;
+    const int row = mb * 128 + 16 * m2 + m0;  // its partner row + 8 is valid with it
+    word = (row < m && kr < k)
+               ? k16[static_cast<long long>(kr / 16) * (m / 2) + (mb * 128 + 16 * m2) / 2 + m0]
+               : 0x44444444u;
   } else {
     const int m2 = L >> 4, k1 = (L >> 3) & 1, m0 = L & 7;
     const int kr = ka * 128 + 32 * w + 16 * k1;  // dense K start of the 16-element run

@@ -23,7 +23,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libsp24.so")
 F16, BF16, E4M3 = 0, 1, 2
 # Mixed fp8: A's format first, B's second (kind::f8f6f4 formats may differ).
 E5M2_E4M3, E4M3_E5M2, E5M2 = 3, 4, 5
-META_REF, META_TC = 0, 1
+META_REF, META_TC, META_K16 = 0, 1, 2
 
 STATUS = {
     0: "SP24_OK", 1: "SP24_ERR_SHAPE", 2: "SP24_ERR_ALIGN", 3: "SP24_ERR_NOT_2OF4",
@@ -37,7 +37,7 @@ EXPORTS = [
     "sp24_gemm_workspace_bytes", "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta",
     "sp24_gemm", "sp24_last_kernel_status", "sp24_selftest_timeout", "sp24_amax_f32",
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
-    "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused",
+    "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused", "sp24_repack_meta_k16",
 ]
 
 ACT_NONE, ACT_SILU = 0, 1
@@ -99,6 +99,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_prune_2of4.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
                                     c_void_p]
     lib.sp24_repack_meta.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+    lib.sp24_repack_meta_k16.argtypes = [c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
     lib.sp24_amax_f32.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p]
     lib.sp24_quantize_e4m3.argtypes = [c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
                                        c_void_p]
@@ -111,7 +112,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                              c_void_p]
     for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_gemm_fused", "sp24_selftest_timeout",
                  "sp24_last_kernel_status",
-                 "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_amax_f32",
+                 "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_repack_meta_k16",
+                 "sp24_amax_f32",
                  "sp24_quantize_e4m3", "sp24_quantize_e5m2", "sp24_unshard_columns_f32",
                  "sp24_check_device"):
         getattr(lib, name).restype = c_int
@@ -196,6 +198,16 @@ def repack_meta(meta_ref, m: int, k: int, dtype, stream=None):
     out = torch.empty(meta_tc_bytes(m, k), dtype=torch.uint8, device=meta_ref.device)
     _check(lib.sp24_repack_meta(dtype_code(dtype), _ptr(meta_ref), m, k, _ptr(out),
                                 _stream(stream)), "sp24_repack_meta")
+    return out
+
+
+def repack_meta_k16(meta_k16, m: int, k: int, dtype, stream=None):
+    """tcgen05 image from metadata in the reference's m16n8k16 layout."""
+    import torch
+    lib = load()
+    out = torch.empty(meta_tc_bytes(m, k), dtype=torch.uint8, device=meta_k16.device)
+    _check(lib.sp24_repack_meta_k16(dtype_code(dtype), _ptr(meta_k16), m, k, _ptr(out),
+                                    _stream(stream)), "sp24_repack_meta_k16")
     return out
 
 

@@ -15,7 +15,10 @@ plus known-answer compressions of an alternating six-pattern matrix for each
 dtype (pins the e4m3 nibble table of wgmma_sp_raw_common.hpp:176-193), and
 every case of the reference's mixed fp8 entry point mma_sp_m16n8k64_fp32fp8.cu
 (A e5m2, B e4m3; through oracle/_ref/libsp24ref_fp8.so): dense A, B (row-major
-K x N), A_c, metadata bytes and its fp32 CPU GEMM.
+K x N), A_c, metadata bytes and its fp32 CPU GEMM; and sha256 records of the
+reference's four legacy warp-level entry points (mma_sp_m16n8k{16,32}_fp32
+{fp16,bf16}.cu, through oracle/_ref/libsp24ref_legacy.so) at a small size and
+at their own 2048^3 size.
 The CuTe harness (wgmma_sp_demo_common.hpp) shares these host algorithms;
 its suites are recorded the same way.
 
@@ -115,8 +118,27 @@ def main() -> None:
                       "k": 64, "a": "e5m2", "b": "e4m3", "tags": s["tags"],
                       "sha256": {key: sha(s[key]) for key in ("a", "b", "a_c", "meta", "c")}}
 
+    # The legacy warp-level entry points (m16n8k16 / m16n8k32, fp16 / bf16):
+    # each main replayed by its own host code at a small size (every array
+    # hashed, C included) and at its own 2048^3 size (A, B, A_c and metadata
+    # hashed; its CPU product is too slow to record here).
+    legacy_mma_sp = None
+    if oracle.ref_legacy_available():
+        legacy_mma_sp = []
+        for which, entry in enumerate(oracle.LEGACY_FILES):
+            rec = {"entry": entry, "which": which, "dtype": oracle.legacy_dtype(which),
+                   "seed": 42, "sizes": []}
+            for (m, n, k, with_c) in ((64, 64, 128, True), (2048, 2048, 2048, False)):
+                a, b, ac, e, c = oracle.ref_legacy_case(which, m, n, k, with_c)
+                h = {"a": sha(a), "b": sha(b), "a_c": sha(ac), "meta_words": sha(e)}
+                if with_c:
+                    h["c"] = sha(c)
+                rec["sizes"].append({"m": m, "n": n, "k": k, "sha256": h})
+            legacy_mma_sp.append(rec)
+
     out = {"generator": "tests/golden/make_golden.py", "reference_seed": 1234,
-           "suites": suites, "kats": kats, "legacy_fp8": legacy_fp8}
+           "suites": suites, "kats": kats, "legacy_fp8": legacy_fp8,
+           "legacy_mma_sp": legacy_mma_sp}
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(out, f, indent=1)
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)

@@ -76,6 +76,10 @@ def _desc(**kw):
     (dict(meta=0x20004), 2),
     (dict(tile_n=300), 8),
     (dict(meta_format=sp24.META_REF), 9),  # reference metadata needs a workspace
+    (dict(meta_format=sp24.META_K16), 9),  # so does the m16n8k16 layout
+    (dict(meta_format=sp24.META_K16, dtype=2, k=128), 1),   # 16-bit types only
+    (dict(meta_format=sp24.META_K16, m=120), 1),            # whole 16-row blocks
+    (dict(meta_format=3), 8),
 ])
 def test_gemm_rejects_bad_descriptors_before_cuda(kw, code):
     lib = sp24.load()

@@ -347,6 +347,44 @@ def test_e4m3_quantize_and_scaled_gemm():
     assert err <= TOL[2], err
 
 
+# ------------------------------------------------------------------ legacy warp-level entry points
+@pytest.mark.parametrize("which", range(4))
+def test_legacy_entry_points_full_size(which):
+    """The workload of each legacy main (mma_sp_m16n8k{16,32}_fp32{fp16,bf16}.cu:
+    2048^3, mt19937(42) in that main's order; the oracle's replay is pinned to
+    the reference by hashes) through sp24_gemm with the main's own metadata
+    layout: m16n8k16 words as SP24_META_K16, m16n8k32 words as SP24_META_REF.
+    GPU compression bit-exact; the k16 repack equals the reference-byte
+    repack; C on 32 sampled rows within the mains' own rule (|dC| <= 0.1)
+    and the row-norm bound."""
+    m = n = k = 2048
+    dt = oracle.legacy_dtype(which)
+    a, b = oracle.gen_legacy(which, m, n, k)
+    ac_ref, e_ref = oracle.compress(dt, a)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    np.testing.assert_array_equal(to_host_bits(ac_t), ac_ref)
+    np.testing.assert_array_equal(e_t.cpu().numpy(), e_ref)
+    if which < 2:
+        words = oracle.meta_k16_from_ref(e_ref, m, k)
+        w_t = torch.from_numpy(words.view(np.int32)).to(DEV)
+        img_k16 = sp24.repack_meta_k16(w_t, m, k, lib_dtype(dt))
+        img_ref = sp24.repack_meta(e_t, m, k, lib_dtype(dt))
+        torch.cuda.synchronize()
+        assert torch.equal(img_k16, img_ref)
+        fmt = sp24.META_K16
+    else:
+        w_t = torch.from_numpy(e_ref.view(np.int32).reshape(m, k // 32).copy()).to(DEV)
+        fmt = sp24.META_REF
+    c, _ = sp24.gemm(ac_t, w_t, to_dev(b, dt), m, n, k, meta_format=fmt, dtype=lib_dtype(dt))
+    torch.cuda.synchronize()
+    rows = np.sort(np.random.default_rng(which).choice(m, 32, replace=False))
+    ref = oracle.gemm(dt, a[rows], b, threads=8)
+    got = c[rows].cpu().numpy()
+    assert np.abs(got - ref).max() <= 0.1
+    err = oracle.row_norm_rel_error(got, ref, oracle.to_float(dt, a[rows]), oracle.to_float(dt, b))
+    assert err <= 1e-2, err
+
+
 # ------------------------------------------------------------------ mixed fp8
 def test_legacy_fp8_suite_on_gpu(golden):
     """Every case of the reference's mixed fp8 entry point

@@ -201,3 +201,31 @@ def test_quantize_e5m2_scale_and_saturation():
     back = oracle.to_float(oracle.E5M2, q) / s
     assert abs(back[1, 0] - 7.0) < 1e-6 and abs(back[1, 1] + 7.0) < 1e-6
     assert q[0, 0] == 0
+
+
+# ------------------------------------------------------------------ legacy warp-level entry points
+@pytest.mark.parametrize("which", range(4))
+def test_legacy_mma_sp_oracle_matches_reference(golden, which):
+    """The reference's m16n8k16 / m16n8k32 mains (fp16, bf16) replayed by the
+    oracle: their mt19937(42) generation order, the compression, the
+    m16n8k16 word packing (the m16n8k32 words are the reference bytes read
+    little-endian) and the fp32 CPU product hash to what the reference's own
+    host code produced, at a small size and at the mains' 2048^3."""
+    meta, _ = golden
+    rec = meta["legacy_mma_sp"][which]
+    assert rec["entry"] == oracle.LEGACY_FILES[which]
+    dt = oracle.legacy_dtype(which)
+
+    def sha(x):
+        return hashlib.sha256(np.ascontiguousarray(x).tobytes()).hexdigest()
+
+    for size in rec["sizes"]:
+        m, n, k, h = size["m"], size["n"], size["k"], size["sha256"]
+        a, b = oracle.gen_legacy(which, m, n, k)
+        assert sha(a) == h["a"] and sha(b) == h["b"]
+        ac, e = oracle.compress(dt, a)
+        assert sha(ac) == h["a_c"]
+        words = oracle.meta_k16_from_ref(e, m, k) if which < 2 else e.view(np.uint32)
+        assert sha(words) == h["meta_words"]
+        if "c" in h:
+            assert sha(oracle.gemm(dt, a, b)) == h["c"]
