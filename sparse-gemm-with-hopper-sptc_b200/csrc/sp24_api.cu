@@ -856,15 +856,19 @@ sp24_status sp24_compress(sp24_dtype dtype, const void* a_dense, int m, int k, i
     return SP24_ERR_ALIGN;
   cudaStream_t s = as_stream(stream);
   SP24_CUDA_TRY(cudaMemsetAsync(bad_dev, 0xFF, sizeof(long long), s));
+  const int chunks_per_thread = 4;                  // compress_kernel's U
   const long long work = static_cast<long long>(m) * (k / 8);
-  const unsigned int g = grid_for(work, 256);
+  // The kernel indexes units with 32-bit arithmetic (work plus one block's span).
+  if (work + static_cast<long long>(sp24::kPrepThreads) * chunks_per_thread >= (1LL << 32))
+    return SP24_ERR_SHAPE;
+  const unsigned int g = grid_for(work, sp24::kPrepThreads * chunks_per_thread);
   auto* bad = reinterpret_cast<unsigned long long*>(bad_dev);
   const auto* a8 = static_cast<const uint8_t*>(a_dense);
   auto* c8 = static_cast<uint8_t*>(a_c);
   if (es == 2)
-    sp24::compress_kernel<2><<<g, 256, 0, s>>>(a8, m, k, lda * 2, c8, ldac * 2, meta_ref, bad);
+    sp24::compress_kernel<2><<<g, sp24::kPrepThreads, 0, s>>>(a8, m, k, lda * 2, c8, ldac * 2, meta_ref, bad);
   else
-    sp24::compress_kernel<1><<<g, 256, 0, s>>>(a8, m, k, lda, c8, ldac, meta_ref, bad);
+    sp24::compress_kernel<1><<<g, sp24::kPrepThreads, 0, s>>>(a8, m, k, lda, c8, ldac, meta_ref, bad);
   SP24_CUDA_TRY(cudaGetLastError());
   long long h = -1;
   SP24_CUDA_TRY(cudaMemcpyAsync(&h, bad_dev, sizeof(long long), cudaMemcpyDeviceToHost, s));
@@ -886,16 +890,19 @@ sp24_status sp24_prune_2of4(sp24_dtype dtype, const void* a, int m, int k, int64
       (lda * es) % need || (ldp * es) % need)
     return SP24_ERR_ALIGN;
   cudaStream_t s = as_stream(stream);
+  const int groups_per_thread = 8;                  // prune_kernel's U
   const long long work = static_cast<long long>(m) * (k / 4);
-  const unsigned int g = grid_for(work, 256);
+  if (work + static_cast<long long>(sp24::kPrepThreads) * groups_per_thread >= (1LL << 32))
+    return SP24_ERR_SHAPE;
+  const unsigned int g = grid_for(work, sp24::kPrepThreads * groups_per_thread);
   const auto* a8 = static_cast<const uint8_t*>(a);
   auto* p8 = static_cast<uint8_t*>(a_pruned);
   if (dtype == SP24_F16)
-    sp24::prune_kernel<0><<<g, 256, 0, s>>>(a8, m, k, lda * 2, p8, ldp * 2);
+    sp24::prune_kernel<0><<<g, sp24::kPrepThreads, 0, s>>>(a8, m, k, lda * 2, p8, ldp * 2);
   else if (dtype == SP24_BF16)
-    sp24::prune_kernel<1><<<g, 256, 0, s>>>(a8, m, k, lda * 2, p8, ldp * 2);
+    sp24::prune_kernel<1><<<g, sp24::kPrepThreads, 0, s>>>(a8, m, k, lda * 2, p8, ldp * 2);
   else
-    sp24::prune_kernel<2><<<g, 256, 0, s>>>(a8, m, k, lda, p8, ldp);
+    sp24::prune_kernel<2><<<g, sp24::kPrepThreads, 0, s>>>(a8, m, k, lda, p8, ldp);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
 }
@@ -943,7 +950,10 @@ sp24_status sp24_amax_f32(const float* x, size_t count, float* amax_dev, sp24_st
   if (st != SP24_OK) return st;
   const unsigned int g = std::min<unsigned int>(grid_for(static_cast<long long>(count), 256),
                                                 static_cast<unsigned int>(di->sm_count) * 8u);
-  sp24::amax_kernel<<<g, 256, 0, s>>>(x, count, amax_dev);
+  if (aligned16(x))
+    sp24::amax_kernel<1><<<g, 256, 0, s>>>(x, count, amax_dev);
+  else
+    sp24::amax_kernel<0><<<g, 256, 0, s>>>(x, count, amax_dev);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
 }
@@ -962,7 +972,10 @@ sp24_status quantize_fp8(const float* x, size_t count, const float* amax_dev, fl
   cudaStream_t s = as_stream(stream);
   const unsigned int g = std::min<unsigned int>(grid_for(static_cast<long long>(count), 256),
                                                 static_cast<unsigned int>(di->sm_count) * 16u);
-  sp24::quantize_fp8_kernel<E5M2><<<g, 256, 0, s>>>(x, count, amax_dev, scale_dev, q);
+  if (aligned16(x) && (reinterpret_cast<uintptr_t>(q) & 3u) == 0)
+    sp24::quantize_fp8_kernel<E5M2, 1><<<g, 256, 0, s>>>(x, count, amax_dev, scale_dev, q);
+  else
+    sp24::quantize_fp8_kernel<E5M2, 0><<<g, 256, 0, s>>>(x, count, amax_dev, scale_dev, q);
   SP24_CUDA_TRY(cudaGetLastError());
   return SP24_OK;
 }

@@ -42,100 +42,182 @@ __device__ __forceinline__ float mag_bits(uint32_t v) {
   }
 }
 
-// One thread per chunk of 8 dense elements (two groups -> one metadata byte).
-// ESZ = element bytes; elements are moved as raw bits so values stay bit-exact.
-template <int ESZ>
-__global__ void compress_kernel(const uint8_t* __restrict__ a, int m, int k, long long lda_b,
-                                uint8_t* __restrict__ ac, long long ldac_b,
-                                uint8_t* __restrict__ meta, unsigned long long* __restrict__ bad) {
-  const int chunks = k / 8;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<long long>(m) * chunks) return;
-  const int row = static_cast<int>(idx / chunks);
-  const int ch = static_cast<int>(idx - static_cast<long long>(row) * chunks);
-  const uint8_t* src = a + row * lda_b + static_cast<long long>(ch) * 8 * ESZ;
-  uint32_t e[8];
-  if constexpr (ESZ == 2) {
-    const uint4 v = *reinterpret_cast<const uint4*>(src);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) e[2 * i] = w[i] & 0xFFFFu, e[2 * i + 1] = w[i] >> 16;
-  } else {
-    const uint2 v = *reinterpret_cast<const uint2*>(src);
-    const uint32_t w[2] = {v.x, v.y};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) e[i] = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+// Work split of the byte-moving kernels: a block of kPrepThreads threads owns
+// kPrepThreads * U consecutive units (row-major over the matrix) and thread t
+// takes units t, t + kPrepThreads, ..., so every load instruction of a warp
+// covers consecutive units (coalesced) while each thread keeps U loads in
+// flight before it computes.  The unit's (row, column) comes from one
+// division for the first unit and is stepped forward for the others.
+constexpr int kPrepThreads = 256;
+
+struct UnitCursor {
+  int row, col;
+  __device__ __forceinline__ UnitCursor(unsigned first, unsigned per_row)
+      : row(static_cast<int>(first / per_row)),
+        col(static_cast<int>(first - static_cast<unsigned>(first / per_row) * per_row)) {}
+  __device__ __forceinline__ void advance(int per_row) {
+    col += kPrepThreads;
+    while (col >= per_row) col -= per_row, ++row;
   }
-  uint32_t out[4];
-  uint32_t nib[2];
+};
+
+// Metadata code of a group from its 4-bit nonzero mask (bit j: element j is
+// nonzero): i0 | i1 << 2 for the six masks with two bits set, 0 (never a
+// valid code) for the others.
+constexpr unsigned long long kCodeOfMask =
+    (0x4ull << (4 * 3)) | (0x8ull << (4 * 5)) | (0x9ull << (4 * 6)) | (0xCull << (4 * 9)) |
+    (0xDull << (4 * 10)) | (0xEull << (4 * 12));
+
+// Nonzero masks of the two 16-bit lanes of w (bit 0: low lane) and of the four
+// 8-bit lanes of w, where "nonzero" is any bit other than the sign set.
+__device__ __forceinline__ uint32_t nz_mask16(uint32_t w) {
+  const uint32_t t = w & 0x7FFF7FFFu;
+  const uint32_t h = ((t + 0x7FFF7FFFu) | t) & 0x80008000u;
+  return (h >> 15 & 1u) | (h >> 30 & 2u);
+}
+__device__ __forceinline__ uint32_t nz_mask8(uint32_t w) {
+  const uint32_t t = w & 0x7F7F7F7Fu;
+  const uint32_t h = (((t + 0x7F7F7F7Fu) | t) & 0x80808080u) >> 7;
+  return (h | h >> 7 | h >> 14 | h >> 21) & 0xFu;
+}
+
+// One unit = a chunk of 8 dense elements (two groups -> one metadata byte).
+// ESZ = element bytes; elements move as raw bits so values stay bit-exact.
+template <int ESZ>
+__global__ void __launch_bounds__(kPrepThreads)
+    compress_kernel(const uint8_t* __restrict__ a, int m, int k, long long lda_b,
+                    uint8_t* __restrict__ ac, long long ldac_b, uint8_t* __restrict__ meta,
+                    unsigned long long* __restrict__ bad) {
+  constexpr int U = 4;
+  const int chunks = k / 8;
+  const unsigned total = static_cast<unsigned>(m) * static_cast<unsigned>(chunks);
+  const unsigned first = blockIdx.x * kPrepThreads * U + threadIdx.x;
+  if (first >= total) return;
+  // Each chunk as 16-bit lanes (ESZ 2: four words) or 8-bit lanes (ESZ 1: two words).
+  uint32_t w[U][4];
+  UnitCursor cur(first, static_cast<unsigned>(chunks));
+  int rows[U], cols[U];
 #pragma unroll
-  for (int g = 0; g < 2; ++g) {
-    int i0 = -1, i1 = -1, nz = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (nz_bits<ESZ>(e[4 * g + i])) {
-        if (nz == 0) i0 = i;
-        else if (nz == 1) i1 = i;
-        ++nz;
+  for (int u = 0; u < U; ++u) {
+    rows[u] = -1;
+    if (first + static_cast<unsigned>(u) * kPrepThreads < total) {
+      rows[u] = cur.row;
+      cols[u] = cur.col;
+      const uint8_t* src = a + cur.row * lda_b + static_cast<long long>(cur.col) * 8 * ESZ;
+      if constexpr (ESZ == 2) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src);
+        w[u][0] = v.x, w[u][1] = v.y, w[u][2] = v.z, w[u][3] = v.w;
+      } else {
+        const uint2 v = *reinterpret_cast<const uint2*>(src);
+        w[u][0] = v.x, w[u][1] = v.y;
       }
     }
-    if (nz != 2) {
-      atomicMin(bad, static_cast<unsigned long long>(row) * (k / 4) + 2 * ch + g);
-      i0 = 0, i1 = 1;  // keep going; the call reports the error
+    cur.advance(chunks);
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (rows[u] < 0) break;
+    const int row = rows[u], ch = cols[u];
+    uint32_t code[2], packed[2];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      uint32_t mask;
+      if constexpr (ESZ == 2) mask = nz_mask16(w[u][2 * g]) | (nz_mask16(w[u][2 * g + 1]) << 2);
+      else mask = nz_mask8(w[u][g]);
+      uint32_t c = static_cast<uint32_t>(kCodeOfMask >> (4 * mask)) & 0xFu;
+      if (c == 0) {
+        atomicMin(bad, static_cast<unsigned long long>(row) * (k / 4) + 2 * ch + g);
+        c = 0x4u;  // keep going with positions 0, 1; the call reports the error
+      }
+      const uint32_t i0 = c & 3u, i1 = c >> 2;
+      if constexpr (ESZ == 2) {
+        const uint32_t lo = w[u][2 * g], hi = w[u][2 * g + 1];
+        const uint32_t e0 = ((i0 < 2 ? lo : hi) >> (16 * (i0 & 1))) & 0xFFFFu;
+        const uint32_t e1 = ((i1 < 2 ? lo : hi) >> (16 * (i1 & 1))) & 0xFFFFu;
+        packed[g] = e0 | (e1 << 16);
+      } else {
+        const uint32_t x = w[u][g];
+        packed[g] = ((x >> (8 * i0)) & 0xFFu) | (((x >> (8 * i1)) & 0xFFu) << 8);
+      }
+      code[g] = c;
     }
-    out[2 * g] = e[4 * g + i0];
-    out[2 * g + 1] = e[4 * g + i1];
-    nib[g] = static_cast<uint32_t>(i0 | (i1 << 2));
+    uint8_t* dst = ac + row * ldac_b + static_cast<long long>(ch) * 4 * ESZ;
+    if constexpr (ESZ == 2) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = packed[0] | (packed[1] << 16);
+    }
+    meta[static_cast<long long>(row) * (k / 8) + ch] = static_cast<uint8_t>(code[0] | (code[1] << 4));
   }
-  uint8_t* dst = ac + row * ldac_b + static_cast<long long>(ch) * 4 * ESZ;
-  if constexpr (ESZ == 2) {
-    *reinterpret_cast<uint2*>(dst) = make_uint2(out[0] | (out[1] << 16), out[2] | (out[3] << 16));
-  } else {
-    *reinterpret_cast<uint32_t*>(dst) = out[0] | (out[1] << 8) | (out[2] << 16) | (out[3] << 24);
-  }
-  meta[static_cast<long long>(row) * (k / 8) + ch] = static_cast<uint8_t>(nib[0] | (nib[1] << 4));
 }
 
 // Magnitude pruning: keep the two largest |x| per group of four; ties keep
-// the lower index; the other two become +0.
+// the lower index; the other two become +0.  One unit = one group of four.
+// Element j survives when fewer than two others beat it (larger magnitude,
+// or equal magnitude at a lower index): six comparisons, no branches.
 template <int DT>
-__global__ void prune_kernel(const uint8_t* __restrict__ a, int m, int k, long long lda_b,
-                             uint8_t* __restrict__ p, long long ldp_b) {
+__global__ void __launch_bounds__(kPrepThreads)
+    prune_kernel(const uint8_t* __restrict__ a, int m, int k, long long lda_b,
+                 uint8_t* __restrict__ p, long long ldp_b) {
   constexpr int ESZ = DT == 2 ? 1 : 2;
+  constexpr int U = 8;
   const int groups = k / 4;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<long long>(m) * groups) return;
-  const int row = static_cast<int>(idx / groups);
-  const int g = static_cast<int>(idx - static_cast<long long>(row) * groups);
-  const uint8_t* src = a + row * lda_b + static_cast<long long>(g) * 4 * ESZ;
-  uint32_t e[4];
-  if constexpr (ESZ == 2) {
-    const uint2 v = *reinterpret_cast<const uint2*>(src);
-    e[0] = v.x & 0xFFFFu, e[1] = v.x >> 16, e[2] = v.y & 0xFFFFu, e[3] = v.y >> 16;
-  } else {
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(src);
+  const unsigned total = static_cast<unsigned>(m) * static_cast<unsigned>(groups);
+  const unsigned first = blockIdx.x * kPrepThreads * U + threadIdx.x;
+  if (first >= total) return;
+  uint32_t w[U][2];
+  UnitCursor cur(first, static_cast<unsigned>(groups));
+  int rows[U], cols[U];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) e[i] = (v >> (8 * i)) & 0xFFu;
+  for (int u = 0; u < U; ++u) {
+    rows[u] = -1;
+    if (first + static_cast<unsigned>(u) * kPrepThreads < total) {
+      rows[u] = cur.row;
+      cols[u] = cur.col;
+      const uint8_t* src = a + cur.row * lda_b + static_cast<long long>(cur.col) * 4 * ESZ;
+      if constexpr (ESZ == 2) {
+        const uint2 v = *reinterpret_cast<const uint2*>(src);
+        w[u][0] = v.x, w[u][1] = v.y;
+      } else {
+        w[u][0] = *reinterpret_cast<const uint32_t*>(src);
+      }
+    }
+    cur.advance(groups);
   }
-  float mg[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) mg[i] = mag_bits<DT>(e[i]);
-  int b0 = 0;
+  for (int u = 0; u < U; ++u) {
+    if (rows[u] < 0) break;
+    uint32_t e[4];
+    if constexpr (ESZ == 2) {
+      e[0] = w[u][0] & 0xFFFFu, e[1] = w[u][0] >> 16, e[2] = w[u][1] & 0xFFFFu, e[3] = w[u][1] >> 16;
+    } else {
 #pragma unroll
-  for (int i = 1; i < 4; ++i)
-    if (mg[i] > mg[b0]) b0 = i;
-  int b1 = (b0 == 0) ? 1 : 0;
+      for (int i = 0; i < 4; ++i) e[i] = (w[u][0] >> (8 * i)) & 0xFFu;
+    }
+    float mg[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    if (i != b0 && mg[i] > mg[b1]) b1 = i;
-  uint8_t* dst = p + row * ldp_b + static_cast<long long>(g) * 4 * ESZ;
-  uint32_t o[4];
+    for (int i = 0; i < 4; ++i) mg[i] = mag_bits<DT>(e[i]);
+    int beaten[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) o[i] = (i == b0 || i == b1) ? e[i] : 0u;
-  if constexpr (ESZ == 2) {
-    *reinterpret_cast<uint2*>(dst) = make_uint2(o[0] | (o[1] << 16), o[2] | (o[3] << 16));
-  } else {
-    *reinterpret_cast<uint32_t*>(dst) = o[0] | (o[1] << 8) | (o[2] << 16) | (o[3] << 24);
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = i + 1; j < 4; ++j) {
+        // i < j: i wins ties.
+        const int jw = mg[j] > mg[i] ? 1 : 0;
+        beaten[i] += jw;
+        beaten[j] += 1 - jw;
+      }
+    uint8_t* dst = p + rows[u] * ldp_b + static_cast<long long>(cols[u]) * 4 * ESZ;
+    if constexpr (ESZ == 2) {
+      const uint32_t k0 = (beaten[0] < 2 ? 0xFFFFu : 0u) | (beaten[1] < 2 ? 0xFFFF0000u : 0u);
+      const uint32_t k1 = (beaten[2] < 2 ? 0xFFFFu : 0u) | (beaten[3] < 2 ? 0xFFFF0000u : 0u);
+      *reinterpret_cast<uint2*>(dst) = make_uint2(w[u][0] & k0, w[u][1] & k1);
+    } else {
+      uint32_t keep = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) keep |= (beaten[i] < 2 ? 0xFFu : 0u) << (8 * i);
+      *reinterpret_cast<uint32_t*>(dst) = w[u][0] & keep;
+    }
   }
 }
 
@@ -204,11 +286,35 @@ __global__ void repack_meta_kernel(const uint8_t* __restrict__ ref, int m, int k
   img[idx] = word;
 }
 
+// max |x| over n floats.  VEC: x is 16-byte aligned; each thread then reads
+// four float4 per step (64 bytes in flight), the tail n % 4 is read by
+// thread 0 of block 0.
+template <int VEC>
 __global__ void amax_kernel(const float* __restrict__ x, size_t n, float* __restrict__ amax) {
   float v = 0.f;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    v = fmaxf(v, fabsf(x[i]));
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if constexpr (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const size_t n4 = n / 4;
+    size_t i = tid;
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = x4[i + u * stride];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v = fmaxf(v, fmaxf(fmaxf(fabsf(q[u].x), fabsf(q[u].y)), fmaxf(fabsf(q[u].z), fabsf(q[u].w))));
+    }
+    for (; i < n4; i += stride) {
+      const float4 q = x4[i];
+      v = fmaxf(v, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+    }
+    if (tid == 0)
+      for (size_t t = n4 * 4; t < n; ++t) v = fmaxf(v, fabsf(x[t]));
+  } else {
+    for (size_t i = tid; i < n; i += stride) v = fmaxf(v, fabsf(x[i]));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   __shared__ float red[32];
@@ -225,7 +331,9 @@ __global__ void amax_kernel(const float* __restrict__ x, size_t n, float* __rest
 
 // Per-tensor fp8 quantisation: scale = largest finite value / amax
 // (448 for e4m3, 57344 for e5m2), q = fp8_rn_satfinite(x * scale).
-template <int E5M2>
+// VEC: x 16-byte aligned and q 4-byte aligned; a thread converts four float4
+// per step (64 bytes in flight) and writes each as one 4-byte word.
+template <int E5M2, int VEC>
 __global__ void quantize_fp8_kernel(const float* __restrict__ x, size_t n,
                                     const float* __restrict__ amax, float* __restrict__ scale_out,
                                     uint8_t* __restrict__ q) {
@@ -234,9 +342,33 @@ __global__ void quantize_fp8_kernel(const float* __restrict__ x, size_t n,
   const float am = amax[0];
   const float s = am > 0.f ? kMax / am : 1.0f;
   if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out != nullptr) scale_out[0] = s;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    q[i] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(x[i] * s, __NV_SATFINITE, kFmt));
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  auto cvt = [&](float f) -> uint32_t {
+    return static_cast<uint32_t>(__nv_cvt_float_to_fp8(f * s, __NV_SATFINITE, kFmt));
+  };
+  if constexpr (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    uint32_t* q4 = reinterpret_cast<uint32_t*>(q);
+    const size_t n4 = n / 4;
+    size_t i = tid;
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 f[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) f[u] = x4[i + u * stride];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        q4[i + u * stride] = cvt(f[u].x) | (cvt(f[u].y) << 8) | (cvt(f[u].z) << 16) | (cvt(f[u].w) << 24);
+    }
+    for (; i < n4; i += stride) {
+      const float4 f = x4[i];
+      q4[i] = cvt(f.x) | (cvt(f.y) << 8) | (cvt(f.z) << 16) | (cvt(f.w) << 24);
+    }
+    if (tid == 0)
+      for (size_t t = n4 * 4; t < n; ++t) q[t] = static_cast<uint8_t>(cvt(x[t]));
+  } else {
+    for (size_t i = tid; i < n; i += stride) q[i] = static_cast<uint8_t>(cvt(x[i]));
+  }
 }
 
 // dst[r][c] = shard(c)[r][c - n0(shard)] where shard r's block starts at
