@@ -10,7 +10,7 @@ and no collective runs on the GEMM path -> weak scaling, value = total
 dense-equivalent FLOPs of all ranks / max-over-ranks time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sp24|reference]
-                    [--config 2|3|4|5] [--allgather]
+                    [--config 2|3|4|5] [--allgather [nccl|fused|both]]
                     [--config 4 --layer up|down --tokens 8|16|64|128|4096]
 
 Configuration 4 (the MLP layers) at T <= 128 tokens is bound by HBM: its
@@ -288,7 +288,11 @@ def main():
     ap.add_argument("--impl", default="sp24", choices=["sp24", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--allgather", action="store_true")
+    ap.add_argument("--allgather", nargs="?", const="nccl", default=None,
+                    choices=["nccl", "fused", "both"],
+                    help="also time a replicated C after the GEMM: nccl = all-gather of the "
+                         "shards + column permute; fused = sp24_gemm_allgather (peer stores "
+                         "over NVLink inside the GEMM)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--tokens", type=int, default=4096,
@@ -448,7 +452,7 @@ def main():
     # Optional replicated output: all-gather of the C shards over NVLink,
     # timed separately from the GEMM (config 5 option).
     allgather = None
-    if args.allgather and world > 1 and c32 is not None:
+    if args.allgather in ("nccl", "both") and world > 1 and c32 is not None:
         flat = c32.reshape(-1)
         out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=dev)
         dist.all_gather_into_tensor(out, flat)
@@ -476,6 +480,63 @@ def main():
                      "unshard_ms": ta[1].item(), "bytes_received_per_rank": recv,
                      "nccl_GB_per_s_per_rank": recv / (ta[0].item() * 1e-3) / 1e9}
         del out, full
+
+    # Fused alternative: every rank's GEMM stores its shard into all ranks'
+    # full C over NVLink (CUDA IPC peer pointers); a one-element all-reduce
+    # after each launch is the completion barrier.  Timed per step against
+    # the GEMM alone.
+    fused_ag = None
+    if args.allgather in ("fused", "both") and world > 1 and c32 is not None:
+        full = torch.empty((m, n * world), dtype=torch.float32, device=dev)
+        handle = sp24.ipc_handle(full)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle)
+        opened, peers = {}, []
+        for r in range(world):
+            if r == rank:
+                continue
+            h, off = handles[r]
+            if h not in opened:
+                opened[h] = sp24.ipc_open(h)
+            peers.append(opened[h] + off + rank * n * 4)
+        dfull = sp24.make_desc(ac, img, b, m, n, k, meta_format=sp24.META_TC,
+                               c_f32=full[:, rank * n:(rank + 1) * n], alpha=alpha, dtype=lib_dt)
+        po = sp24.PeerOut()
+        po.n_peers = len(peers)
+        for i, addr in enumerate(peers):
+            po.c_f32[i] = addr
+        tick = torch.zeros(1, device=dev)
+
+        def fused_step():
+            rc = lib.sp24_gemm_allgather(ctypes.byref(dfull), ctypes.byref(po), sptr)
+            if rc != 0:
+                raise sp24.Sp24Error(rc, "sp24_gemm_allgather")
+            dist.all_reduce(tick)
+
+        for _ in range(3):
+            fused_step()
+        torch.cuda.synchronize()
+        barrier()
+        reps = min(args.steps, 20)
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(reps):
+            fused_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        tf_ = torch.tensor([f0.elapsed_time(f1) / reps], device=dev)
+        dist.all_reduce(tf_, op=dist.ReduceOp.MAX)
+        sent = m * n * 4 * (world - 1)
+        fused_ag = {"ms_per_step": tf_.item(), "gemm_only_ms_per_step": ms_step,
+                    "bytes_sent_per_rank": sent,
+                    "tflops": flops_rank * world / (tf_.item() * 1e-3) / 1e12,
+                    "what": "sp24_gemm_allgather (GEMM + peer stores of C over NVLink) + "
+                            "1-element all-reduce barrier, per step"}
+        barrier()
+        for base in opened.values():
+            sp24.ipc_close(base)
+        del full
 
     # End to end through the public C ABI with host buffers.
     e2e = None
@@ -610,6 +671,8 @@ def main():
         }
         if allgather:
             line["allgather"] = allgather
+        if fused_ag:
+            line["fused_allgather"] = fused_ag
         if unfused:
             line["unfused_comparison"] = unfused
         print(json.dumps(line), flush=True)

@@ -235,6 +235,36 @@ sp24_status sp24_quantize_e4m3(const float* x, size_t count, const float* amax_d
 sp24_status sp24_quantize_e5m2(const float* x, size_t count, const float* amax_dev,
                                float* scale_dev, uint8_t* q, sp24_stream_t stream);
 
+/* Fused all-gather of C over NVLink (no counterpart in the reference; it
+   replaces the optional NCCL all-gather of the column shards and the
+   column-block permute after it).  Each rank runs the GEMM of its column shard
+   of C with d->c_f32 / d->c_bf16 pointing at the shard's first column inside
+   the rank's own full M x N_total C (d->ldc = N_total); the kernel stores
+   every finished tile there and, with peer stores over NVLink, at the same
+   element of every peer's full C (peers->c_f32[i] / c_bf16[i]: the peer's
+   buffer, mapped into this process, plus the same element offset).  Kernels
+   never wait on peers.  The gathered C is complete once every rank's call has
+   completed: order that with a barrier across the ranks after the launch
+   (e.g. a one-element NCCL all-reduce on the same streams).
+   Peer pointers must share the local pointer's 32-byte alignment. */
+#define SP24_MAX_PEERS 7
+typedef struct sp24_peer_out {
+  int n_peers;                     /* 0 .. SP24_MAX_PEERS */
+  float* c_f32[SP24_MAX_PEERS];    /* when d->c_f32 is set */
+  void* c_bf16[SP24_MAX_PEERS];    /* when d->c_bf16 is set */
+} sp24_peer_out;
+sp24_status sp24_gemm_allgather(const sp24_gemm_desc* d, const sp24_peer_out* peers,
+                                sp24_stream_t stream);
+
+/* CUDA IPC plumbing for the peer buffers (host calls, no stream work).
+   sp24_ipc_get_handle: 64-byte handle of the allocation holding dev_ptr and
+   the byte offset of dev_ptr inside it.  sp24_ipc_open_handle: maps a peer's
+   handle into this process (peer access enabled) and returns the
+   allocation's base; add the offset.  sp24_ipc_close: unmaps it. */
+sp24_status sp24_ipc_get_handle(const void* dev_ptr, void* handle64, size_t* offset);
+sp24_status sp24_ipc_open_handle(const void* handle64, void** base);
+sp24_status sp24_ipc_close(void* base);
+
 /* Multi-GPU N-sharding helpers (no collective on the GEMM path).
    Columns [n0, n1) of C belong to `rank` of `world`; boundaries are multiples
    of `align` (the tile width) except the last. */

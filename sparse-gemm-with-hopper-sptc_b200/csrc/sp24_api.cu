@@ -79,6 +79,24 @@ sp24_status get_encode_fn() {
   return g_encode ? SP24_OK : SP24_ERR_CUDA;
 }
 
+PFN_cuMemGetAddressRange_v3020 g_range = nullptr;
+
+// cuMemGetAddressRange (the allocation holding a pointer), resolved at run
+// time like the tensor-map encoder.
+sp24_status get_range_fn() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 3020, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    (void)cudaGetLastError();
+  });
+  return g_range ? SP24_OK : SP24_ERR_CUDA;
+}
+
 struct DeviceInfo {
   int sm_count = 0;
   int* status_word = nullptr;
@@ -154,6 +172,7 @@ struct Prepared {
   float alpha_up;
   const float* bias_up;
   int gate_from_c;
+  sp24::PeerOut peers;
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -203,6 +222,7 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.bias = p.bias;
   P.act = p.act;
   P.gate_from_c = p.gate_from_c;
+  P.peers = p.peers;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -272,6 +292,7 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   P.bias = p.bias;
   P.act = p.act;
   P.gate_from_c = p.gate_from_c;
+  P.peers = p.peers;
   P.vec_f32 = p.c_f32 == nullptr                            ? 0
               : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
               : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
@@ -394,6 +415,7 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.bias = p.bias;
   P.act = p.act;
   P.gate_from_c = p.gate_from_c;
+  P.peers = p.peers;
   P.vec_f32 = (p.c_f32 != nullptr && aligned16(p.c_f32) && (p.ldc % 4) == 0) ? 1 : 0;
   P.vec_bf16 = (p.c_bf16 != nullptr && aligned16(p.c_bf16) && (p.ldc % 8) == 0) ? 1 : 0;
   P.status = p.status;
@@ -586,11 +608,35 @@ sp24_status validate_epilogue(const sp24_gemm_desc* d, const sp24_epilogue* e) {
   return SP24_OK;
 }
 
+// Checks of the fused all-gather destinations.
+sp24_status validate_peers(const sp24_gemm_desc* d, const sp24_peer_out* peers) {
+  if (peers == nullptr || peers->n_peers == 0) return SP24_OK;
+  if (peers->n_peers < 0 || peers->n_peers > SP24_MAX_PEERS) return SP24_ERR_ARG;
+  for (int i = 0; i < peers->n_peers; ++i) {
+    if (d->c_f32 != nullptr) {
+      if (peers->c_f32[i] == nullptr) return SP24_ERR_ARG;
+      if ((reinterpret_cast<uintptr_t>(peers->c_f32[i]) & 31u) !=
+          (reinterpret_cast<uintptr_t>(d->c_f32) & 31u))
+        return SP24_ERR_ALIGN;
+    }
+    if (d->c_bf16 != nullptr) {
+      if (peers->c_bf16[i] == nullptr) return SP24_ERR_ARG;
+      if ((reinterpret_cast<uintptr_t>(peers->c_bf16[i]) & 31u) !=
+          (reinterpret_cast<uintptr_t>(d->c_bf16) & 31u))
+        return SP24_ERR_ALIGN;
+    }
+  }
+  return SP24_OK;
+}
+
 sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned long long timeout_ns,
-                      int stall, const sp24_epilogue* e = nullptr) {
+                      int stall, const sp24_epilogue* e = nullptr,
+                      const sp24_peer_out* peers = nullptr) {
   sp24_status st = validate(d);
   if (st != SP24_OK) return st;
   st = validate_epilogue(d, e);
+  if (st != SP24_OK) return st;
+  st = validate_peers(d, peers);
   if (st != SP24_OK) return st;
   const WsPlan w = plan_workspace(d);
   if (w.total > 0 && (d->workspace == nullptr || d->workspace_bytes < w.total))
@@ -615,6 +661,13 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   p.ldc = d->ldc ? d->ldc : d->n;
   p.alpha = d->alpha == 0.0f ? 1.0f : d->alpha;
   p.idesc_ab = idesc_ab(d->dtype);
+  if (peers != nullptr) {
+    p.peers.n = peers->n_peers;
+    for (int i = 0; i < peers->n_peers; ++i) {
+      p.peers.f32[i] = d->c_f32 != nullptr ? peers->c_f32[i] : nullptr;
+      p.peers.bf16[i] = d->c_bf16 != nullptr ? static_cast<__nv_bfloat16*>(peers->c_bf16[i]) : nullptr;
+    }
+  }
   if (e != nullptr) {
     p.bias = e->bias;
     p.act = e->act == SP24_ACT_SILU ? sp24::kActSilu : sp24::kActNone;
@@ -790,6 +843,42 @@ sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream) {
 sp24_status sp24_gemm_fused(const sp24_gemm_desc* d, const sp24_epilogue* e,
                             sp24_stream_t stream) {
   return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0, e);
+}
+
+sp24_status sp24_gemm_allgather(const sp24_gemm_desc* d, const sp24_peer_out* peers,
+                                sp24_stream_t stream) {
+  if (peers == nullptr) return SP24_ERR_ARG;
+  return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0, nullptr, peers);
+}
+
+sp24_status sp24_ipc_get_handle(const void* dev_ptr, void* handle64, size_t* offset) {
+  if (dev_ptr == nullptr || handle64 == nullptr || offset == nullptr) return SP24_ERR_ARG;
+  sp24_status st = get_range_fn();
+  if (st != SP24_OK) return st;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (g_range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return SP24_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  SP24_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle64, &h, sizeof(h));
+  *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return SP24_OK;
+}
+
+sp24_status sp24_ipc_open_handle(const void* handle64, void** base) {
+  if (handle64 == nullptr || base == nullptr) return SP24_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  SP24_CUDA_TRY(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+  return SP24_OK;
+}
+
+sp24_status sp24_ipc_close(void* base) {
+  if (base == nullptr) return SP24_ERR_ARG;
+  SP24_CUDA_TRY(cudaIpcCloseMemHandle(base));
+  return SP24_OK;
 }
 
 sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream) {

@@ -63,6 +63,7 @@ struct PairParams {
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
+  PeerOut peers;
 };
 
 // FINE selects the stage granularity: 0 = 128 dense K per stage for 16-bit
@@ -125,6 +126,9 @@ SP24_DEV void st_global_v8_u32(void* p, const uint32_t* v) {
                : "memory");
 }
 
+SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
+                                const uint32_t (&r)[128], int row, int col0);
+
 // Store 128 consecutive accumulator columns of one row (already in registers).
 SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, int col0) {
   if (row >= P.m) return;
@@ -140,9 +144,55 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
     for (int i = 0; i < 128; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * P.alpha);
   }
   if (P.gate_from_c) gate_mul_row<128>(P, reinterpret_cast<float*>(r), row, col0);
+  pair_store_row_to(P, P.c_f32, P.c_bf16, r, row, col0);
+}
+
+// Fused all-gather, warp-cooperative: after a warp has stored its 32 rows x
+// 128 columns locally (pair_store_row), it re-reads them from L2 with the
+// lanes spread along each row and writes every row segment to the peers as
+// contiguous 512 B (fp32) / 256 B (bf16) runs, i.e. whole 128 B lines over
+// NVLink, instead of one scattered 32 B write per lane and row.
+SP24_DEV void pair_push_rows_to_peers(const PairParams& P, int row0, int col0) {
+  __syncwarp();  // the warp's local stores are visible to its own loads
+  const int lane = threadIdx.x & 31;
   const bool full = col0 + 128 <= P.n;
-  if (P.c_f32 != nullptr) {
-    float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col0;
+  for (int rr = 0; rr < 32; ++rr) {
+    const int row = row0 + rr;
+    if (row >= P.m) break;
+    const long long o = static_cast<long long>(row) * P.ldc + col0;
+    if (P.c_f32 != nullptr) {
+      if (full && P.vec_f32) {
+        const float4 v = *reinterpret_cast<const float4*>(P.c_f32 + o + 4 * lane);
+        for (int p = 0; p < P.peers.n; ++p)
+          *reinterpret_cast<float4*>(P.peers.f32[p] + o + 4 * lane) = v;
+      } else {
+        for (int c = lane; c < 128 && col0 + c < P.n; c += 32) {
+          const float v = P.c_f32[o + c];
+          for (int p = 0; p < P.peers.n; ++p) P.peers.f32[p][o + c] = v;
+        }
+      }
+    }
+    if (P.c_bf16 != nullptr) {
+      if (full && P.vec_bf16) {
+        const uint2 v = *reinterpret_cast<const uint2*>(P.c_bf16 + o + 4 * lane);
+        for (int p = 0; p < P.peers.n; ++p)
+          *reinterpret_cast<uint2*>(P.peers.bf16[p] + o + 4 * lane) = v;
+      } else {
+        for (int c = lane; c < 128 && col0 + c < P.n; c += 32) {
+          const __nv_bfloat16 v = P.c_bf16[o + c];
+          for (int p = 0; p < P.peers.n; ++p) P.peers.bf16[p][o + c] = v;
+        }
+      }
+    }
+  }
+}
+
+// Stores 128 finished values of one row (as float bits) into one copy of C.
+SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
+                                const uint32_t (&r)[128], int row, int col0) {
+  const bool full = col0 + 128 <= P.n;
+  if (c32 != nullptr) {
+    float* dst = c32 + static_cast<long long>(row) * P.ldc + col0;
     if (full && P.vec_f32 == 2) {
 #pragma unroll
       for (int i = 0; i < 128; i += 8) {
@@ -163,8 +213,8 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, i
         if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]);
     }
   }
-  if (P.c_bf16 != nullptr) {
-    __nv_bfloat16* dst = P.c_bf16 + static_cast<long long>(row) * P.ldc + col0;
+  if (c16 != nullptr) {
+    __nv_bfloat16* dst = c16 + static_cast<long long>(row) * P.ldc + col0;
     if (full && P.vec_bf16 >= 1) {
 #pragma unroll
       for (int i = 0; i < 128; i += 16) {
@@ -444,10 +494,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       if (lane == 0) mbar_arrive_cluster(acce_leader);
       const int row = mp * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
       pair_store_row(P, r, row, nb * 256 + half * 128);
+      if (P.peers.n > 0) pair_push_rows_to_peers(P, row - lane, nb * 256 + half * 128);
       aph ^= 1u;
     }
   }
 
+  if (P.peers.n > 0) __threadfence_system();   // peer stores visible before completion
   tc_fence_before();
   __syncthreads();
   cluster_sync();

@@ -55,6 +55,16 @@ SP24_DEV float epi_value(float acc, float alpha, float bias, bool has_bias, int 
   return act == kActSilu ? silu(v) : v;
 }
 
+// Fused all-gather of C: besides the local output, every finished tile is
+// stored into the other ranks' copies of C (peer pointers to the same element
+// as c_f32 / c_bf16, same row pitch), over NVLink.  n = 0: local output only.
+constexpr int kMaxPeers = 7;
+struct PeerOut {
+  int n;
+  float* f32[kMaxPeers];
+  __nv_bfloat16* bf16[kMaxPeers];
+};
+
 struct GemmParams {
   int m, n, k;
   int m_blocks, n_tiles, k_stages, num_tiles;
@@ -76,6 +86,7 @@ struct GemmParams {
   int* status;   // device word: set to 1 when a bounded wait timed out
   unsigned long long timeout_ns;
   int stall_producer;  // self-test only: producer issues nothing so waits time out
+  PeerOut peers;
 };
 
 template <int DT, int BN>
@@ -136,14 +147,14 @@ SP24_DEV void tile_coords(const GemmParams& P, int t, int& mb, int& nb) {
   nb = r / gm;
 }
 
-// Stores N finished values of one row.  PP: any parameter block with m, n,
-// ldc, c_f32, c_bf16, vec_f32, vec_bf16.
+// Stores N finished values of one row into one copy of C (c32 / c16 with
+// P's pitch and vector rules).
 template <int N, typename PP>
-SP24_DEV void store_values(const PP& P, const float (&v)[N], int row, int col) {
-  if (row >= P.m) return;
+SP24_DEV void store_values_to(const PP& P, float* c32, __nv_bfloat16* c16, const float (&v)[N],
+                              int row, int col) {
   const bool full = (col + N <= P.n);
-  if (P.c_f32 != nullptr) {
-    float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col;
+  if (c32 != nullptr) {
+    float* dst = c32 + static_cast<long long>(row) * P.ldc + col;
     if (full && P.vec_f32) {
 #pragma unroll
       for (int i = 0; i < N; i += 4)
@@ -154,8 +165,8 @@ SP24_DEV void store_values(const PP& P, const float (&v)[N], int row, int col) {
         if (col + i < P.n) dst[i] = v[i];
     }
   }
-  if (P.c_bf16 != nullptr) {
-    __nv_bfloat16* dst = P.c_bf16 + static_cast<long long>(row) * P.ldc + col;
+  if (c16 != nullptr) {
+    __nv_bfloat16* dst = c16 + static_cast<long long>(row) * P.ldc + col;
     if (full && P.vec_bf16) {
 #pragma unroll
       for (int i = 0; i < N; i += 8) {
@@ -176,6 +187,16 @@ SP24_DEV void store_values(const PP& P, const float (&v)[N], int row, int col) {
         if (col + i < P.n) dst[i] = __float2bfloat16_rn(v[i]);
     }
   }
+}
+
+// Stores N finished values of one row into C and, for a fused all-gather,
+// into every peer's copy.  PP: any parameter block with m, n, ldc, c_f32,
+// c_bf16, vec_f32, vec_bf16 and peers.
+template <int N, typename PP>
+SP24_DEV void store_values(const PP& P, const float (&v)[N], int row, int col) {
+  if (row >= P.m) return;
+  store_values_to<N>(P, P.c_f32, P.c_bf16, v, row, col);
+  for (int p = 0; p < P.peers.n; ++p) store_values_to<N>(P, P.peers.f32[p], P.peers.bf16[p], v, row, col);
 }
 
 // Value already in C at (row, col) (f32 output if present, else bf16).
@@ -441,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (P.peers.n > 0) __threadfence_system();   // peer stores visible before completion
   if (threadIdx.x == 0 && abort_sh != 0 && P.status != nullptr) atomicExch(P.status, 1);
 #endif
 }

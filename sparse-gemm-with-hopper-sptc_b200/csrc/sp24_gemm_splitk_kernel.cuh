@@ -71,6 +71,7 @@ struct SplitParams {
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
+  PeerOut peers;
 };
 
 // G: weights streamed per CTA (1 plain, 2 gated).
@@ -141,13 +142,13 @@ SP24_DEV uint32_t split_stage_tx(const SplitParams& P, int g) {
   return static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + C::WEIGHTS * atoms * kAtomBytes);
 }
 
-// Stores four finished values of one row.
+// Stores four finished values of one row into one copy of C.
 template <typename PP>
-SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
-  if (row >= P.m) return;
+SP24_DEV void store_vec4_to(const PP& P, float* c32, __nv_bfloat16* c16, float4 v, int row,
+                            int col) {
   const bool full = col + 4 <= P.n;
-  if (P.c_f32 != nullptr) {
-    float* dst = P.c_f32 + static_cast<long long>(row) * P.ldc + col;
+  if (c32 != nullptr) {
+    float* dst = c32 + static_cast<long long>(row) * P.ldc + col;
     if (full && P.vec_f32) {
       *reinterpret_cast<float4*>(dst) = v;
     } else {
@@ -157,8 +158,8 @@ SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
         if (col + i < P.n) dst[i] = e[i];
     }
   }
-  if (P.c_bf16 != nullptr) {
-    __nv_bfloat16* dst = P.c_bf16 + static_cast<long long>(row) * P.ldc + col;
+  if (c16 != nullptr) {
+    __nv_bfloat16* dst = c16 + static_cast<long long>(row) * P.ldc + col;
     if (full && P.vec_bf16) {
       __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y);
       __nv_bfloat162 h1 = __floats2bfloat162_rn(v.z, v.w);
@@ -173,6 +174,14 @@ SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
         if (col + i < P.n) dst[i] = __float2bfloat16_rn(e[i]);
     }
   }
+}
+
+// ... into C and every peer's copy (fused all-gather).
+template <typename PP>
+SP24_DEV void store_vec4(const PP& P, float4 v, int row, int col) {
+  if (row >= P.m) return;
+  store_vec4_to(P, P.c_f32, P.c_bf16, v, row, col);
+  for (int p = 0; p < P.peers.n; ++p) store_vec4_to(P, P.peers.f32[p], P.peers.bf16[p], v, row, col);
 }
 
 // Grid: (m_blocks * n_tiles * S) CTAs in clusters of S along x; CTA rank r of
@@ -468,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (P.peers.n > 0) __threadfence_system();   // peer stores visible before completion
   if (threadIdx.x == 0 && abort_sh != 0 && P.status != nullptr) atomicExch(P.status, 1);
 #endif
 }

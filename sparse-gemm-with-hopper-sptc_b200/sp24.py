@@ -38,7 +38,9 @@ EXPORTS = [
     "sp24_gemm", "sp24_last_kernel_status", "sp24_selftest_timeout", "sp24_amax_f32",
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
     "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused", "sp24_repack_meta_k16",
+    "sp24_gemm_allgather", "sp24_ipc_get_handle", "sp24_ipc_open_handle", "sp24_ipc_close",
 ]
+MAX_PEERS = 7
 
 ACT_NONE, ACT_SILU = 0, 1
 
@@ -70,6 +72,10 @@ class Epilogue(Structure):
     ]
 
 
+class PeerOut(Structure):
+    _fields_ = [("n_peers", c_int), ("c_f32", c_void_p * 7), ("c_bf16", c_void_p * 7)]
+
+
 _lib = None
 
 
@@ -92,6 +98,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_gemm.argtypes = [POINTER(GemmDesc), c_void_p]
     lib.sp24_gemm_noalloc.argtypes = [POINTER(GemmDesc), c_void_p]
     lib.sp24_gemm_fused.argtypes = [POINTER(GemmDesc), POINTER(Epilogue), c_void_p]
+    lib.sp24_gemm_allgather.argtypes = [POINTER(GemmDesc), POINTER(PeerOut), c_void_p]
+    lib.sp24_ipc_get_handle.argtypes = [c_void_p, c_void_p, POINTER(c_size_t)]
+    lib.sp24_ipc_open_handle.argtypes = [c_void_p, POINTER(c_void_p)]
+    lib.sp24_ipc_close.argtypes = [c_void_p]
     lib.sp24_selftest_timeout.argtypes = [POINTER(GemmDesc), c_ulonglong, c_void_p]
     lib.sp24_last_kernel_status.argtypes = [c_void_p]
     lib.sp24_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
@@ -110,7 +120,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                                        POINTER(c_int)]
     lib.sp24_unshard_columns_f32.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                              c_void_p]
-    for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_gemm_fused", "sp24_selftest_timeout",
+    for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_gemm_fused", "sp24_gemm_allgather",
+                 "sp24_ipc_get_handle", "sp24_ipc_open_handle", "sp24_ipc_close",
+                 "sp24_selftest_timeout",
                  "sp24_last_kernel_status",
                  "sp24_compress", "sp24_prune_2of4", "sp24_repack_meta", "sp24_repack_meta_k16",
                  "sp24_amax_f32",
@@ -281,6 +293,38 @@ def gemm_fused(a_c, meta, b, m, n, k, *, bias=None, act=ACT_NONE, a_c_up=None, m
     _check(lib.sp24_gemm_fused(ctypes.byref(d), ctypes.byref(e), _stream(stream)),
            "sp24_gemm_fused")
     return c_f32, c_bf16
+
+
+def ipc_handle(t):
+    """(64-byte handle, byte offset) of the CUDA allocation holding tensor t."""
+    h = ctypes.create_string_buffer(64)
+    off = c_size_t(0)
+    _check(load().sp24_ipc_get_handle(_ptr(t), h, ctypes.byref(off)), "sp24_ipc_get_handle")
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer's allocation into this process; returns its base address."""
+    base = c_void_p(0)
+    buf = ctypes.create_string_buffer(handle, 64)
+    _check(load().sp24_ipc_open_handle(buf, ctypes.byref(base)), "sp24_ipc_open_handle")
+    return base.value
+
+
+def ipc_close(base: int) -> None:
+    _check(load().sp24_ipc_close(c_void_p(base)), "sp24_ipc_close")
+
+
+def gemm_allgather(desc: GemmDesc, peer_f32=(), peer_bf16=(), stream=None) -> None:
+    """sp24_gemm_allgather with peer element addresses (ints) for each output."""
+    po = PeerOut()
+    po.n_peers = max(len(peer_f32), len(peer_bf16))
+    for i, a in enumerate(peer_f32):
+        po.c_f32[i] = a
+    for i, a in enumerate(peer_bf16):
+        po.c_bf16[i] = a
+    _check(load().sp24_gemm_allgather(ctypes.byref(desc), ctypes.byref(po), _stream(stream)),
+           "sp24_gemm_allgather")
 
 
 def last_kernel_status(stream=None) -> int:
