@@ -287,7 +287,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="sp24", choices=["sp24", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--allgather", nargs="?", const="nccl", default=None,
                     choices=["nccl", "fused", "both"],
                     help="also time a replicated C after the GEMM: nccl = all-gather of the "
@@ -575,37 +575,72 @@ def main():
                "d2h_bytes_per_step": h_c16.numel() * 2, "ms_per_step": ms_e2e,
                "steps": args.e2e_steps, "gpu_launches_per_step": 1}
     elif args.e2e_steps > 0:
+        # Every step copies its inputs (A_c, reference metadata, B) from pinned
+        # host memory, runs sp24_gemm (metadata repack included) and copies C
+        # back.  Steps are pipelined over two buffer sets and three streams so
+        # that step i's D2H overlaps step i+1's H2D (PCIe is full duplex) and
+        # the GEMMs run in between; each step still moves its own bytes.
         h_ac = ac.cpu().pin_memory()
         h_meta = meta.cpu().pin_memory()
         h_b = b.cpu().pin_memory()
-        h_c32 = torch.empty((m, n), dtype=torch.float32).pin_memory() if c32 is not None else None
-        h_c16 = torch.empty((m, n), dtype=torch.bfloat16).pin_memory() if c16 is not None else None
-        d_ac, d_meta, d_b = torch.empty_like(ac), torch.empty_like(meta), torch.empty_like(b)
-        d2 = sp24.make_desc(d_ac, d_meta, d_b, m, n, k, meta_format=sp24.META_REF, c_f32=c32,
-                            c_bf16=c16, alpha=alpha, dtype=lib_dt)
-        ws = torch.empty(max(1, sp24.workspace_bytes(d2)), dtype=torch.uint8, device=dev)
-        d2.workspace, d2.workspace_bytes = ws.data_ptr(), ws.numel()
+        slots = []
+        for _ in range(2):
+            sl = {"ac": torch.empty_like(ac), "meta": torch.empty_like(meta),
+                  "b": torch.empty_like(b),
+                  "c32": torch.empty_like(c32) if c32 is not None else None,
+                  "c16": torch.empty_like(c16) if c16 is not None else None,
+                  "h32": torch.empty((m, n), dtype=torch.float32).pin_memory()
+                  if c32 is not None else None,
+                  "h16": torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+                  if c16 is not None else None}
+            sl["d"] = sp24.make_desc(sl["ac"], sl["meta"], sl["b"], m, n, k,
+                                     meta_format=sp24.META_REF, c_f32=sl["c32"],
+                                     c_bf16=sl["c16"], alpha=alpha, dtype=lib_dt)
+            sl["ws"] = torch.empty(max(1, sp24.workspace_bytes(sl["d"])), dtype=torch.uint8,
+                                   device=dev)
+            sl["d"].workspace, sl["d"].workspace_bytes = sl["ws"].data_ptr(), sl["ws"].numel()
+            sl["ev"] = {x: torch.cuda.Event() for x in ("h2d", "gemm", "d2h")}
+            slots.append(sl)
+        s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        used = [False, False]
 
-        def e2e_step():
-            d_ac.copy_(h_ac, non_blocking=True)
-            d_meta.copy_(h_meta, non_blocking=True)
-            d_b.copy_(h_b, non_blocking=True)
-            rc = lib.sp24_gemm(ctypes.byref(d2), sptr)
+        def e2e_step(i):
+            j = i % 2
+            sl = slots[j]
+            with torch.cuda.stream(s_h2d):
+                if used[j]:
+                    s_h2d.wait_event(sl["ev"]["gemm"])     # step i-2 done reading inputs
+                sl["ac"].copy_(h_ac, non_blocking=True)
+                sl["meta"].copy_(h_meta, non_blocking=True)
+                sl["b"].copy_(h_b, non_blocking=True)
+                sl["ev"]["h2d"].record(s_h2d)
+            stream.wait_event(sl["ev"]["h2d"])
+            if used[j]:
+                stream.wait_event(sl["ev"]["d2h"])         # step i-2 done reading outputs
+            rc = lib.sp24_gemm(ctypes.byref(sl["d"]), sptr)
             if rc != 0:
                 raise sp24.Sp24Error(rc, "sp24_gemm")
-            if h_c32 is not None:
-                h_c32.copy_(c32, non_blocking=True)
-            if h_c16 is not None:
-                h_c16.copy_(c16, non_blocking=True)
+            sl["ev"]["gemm"].record(stream)
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(sl["ev"]["gemm"])
+                if sl["h32"] is not None:
+                    sl["h32"].copy_(sl["c32"], non_blocking=True)
+                if sl["h16"] is not None:
+                    sl["h16"].copy_(sl["c16"], non_blocking=True)
+                sl["ev"]["d2h"].record(s_d2h)
+            used[j] = True
 
-        e2e_step()
+        e2e_step(0)
+        e2e_step(1)
         torch.cuda.synchronize()
         barrier()
         x0 = torch.cuda.Event(enable_timing=True)
         x1 = torch.cuda.Event(enable_timing=True)
         x0.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
+        s_h2d.wait_event(x0)
+        for i in range(args.e2e_steps):
+            e2e_step(i)
+        stream.wait_stream(s_d2h)
         x1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -614,10 +649,12 @@ def main():
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         ms_e2e = te.item() / args.e2e_steps
         h2d = sum(x.numel() * x.element_size() for x in (h_ac, h_meta, h_b))
-        d2h = sum(x.numel() * x.element_size() for x in (h_c32, h_c16) if x is not None)
+        d2h = sum(x.numel() * x.element_size() for x in (slots[0]["h32"], slots[0]["h16"])
+                  if x is not None)
         e2e = {"value": flops_rank * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
-               "steps": args.e2e_steps, "gpu_launches_per_step": 2}
+               "steps": args.e2e_steps, "gpu_launches_per_step": 2,
+               "pipeline": "two buffer sets; step i's D2H overlaps step i+1's H2D"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
