@@ -243,6 +243,48 @@ int group_m_env(int dflt) {
   return v > 0 ? v : dflt;
 }
 
+// Parameter block shared by the CTA-pair kernels; tiles of tile_m x tile_n.
+sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n) {
+  sp24::PairParams P{};
+  P.m = p.m;
+  P.n = p.n;
+  P.k = p.k;
+  P.m_blocks = meta_mblocks(p.m);
+  P.m_pairs = (p.m + tile_m - 1) / tile_m;
+  P.n_tiles = (p.n + tile_n - 1) / tile_n;
+  P.k_stages = (p.k + bkd - 1) / bkd;
+  P.num_tiles = P.m_pairs * P.n_tiles;
+  P.group_m = group_m_env(8);
+  P.c_f32 = p.c_f32;
+  P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
+  P.ldc = p.ldc;
+  P.alpha = p.alpha;
+  P.idesc_ab = p.idesc_ab;
+  P.bias = p.bias;
+  P.act = p.act;
+  P.gate_from_c = p.gate_from_c;
+  P.peers = p.peers;
+  P.vec_f32 = p.c_f32 == nullptr                            ? 0
+              : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
+              : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
+                                                            : 0;
+  P.vec_bf16 = p.c_bf16 == nullptr                          ? 0
+               : (aligned32(p.c_bf16) && (p.ldc % 16) == 0) ? 2
+               : (aligned16(p.c_bf16) && (p.ldc % 8) == 0)  ? 1
+                                                            : 0;
+  P.status = p.status;
+  P.timeout_ns = p.timeout_ns;
+  P.stall_producer = p.stall_producer;
+  return P;
+}
+
+// Metadata image viewed as rows of 256 B: one 2 KB atom = an 8-row box.
+sp24_status encode_meta_rows(CUtensorMap* te, const Prepared& p) {
+  const uint64_t lanes = static_cast<uint64_t>(meta_katoms(p.k)) * meta_mblocks(p.m) * 128;
+  return encode_2d(te, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.meta_tc, 256, lanes * 16 / 256, 256, 256,
+                   8, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 template <int DT, int FINE>
 sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
   using C = sp24::PairCfg<DT, FINE>;
@@ -267,43 +309,10 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
                  static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::BKD,
                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != SP24_OK) return st;
-  const int mblk = meta_mblocks(p.m);
-  const uint64_t lanes = static_cast<uint64_t>(meta_katoms(p.k)) * mblk * 128;
-  // Metadata image viewed as rows of 256 B: one 2 KB atom = an 8-row box.
-  st = encode_2d(&te, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.meta_tc, 256, lanes * 16 / 256, 256, 256,
-                 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+  st = encode_meta_rows(&te, p);
   if (st != SP24_OK) return st;
 
-  sp24::PairParams P{};
-  P.m = p.m;
-  P.n = p.n;
-  P.k = p.k;
-  P.m_blocks = mblk;
-  P.m_pairs = (p.m + 255) / 256;
-  P.n_tiles = (p.n + 255) / 256;
-  P.k_stages = (p.k + C::BKD - 1) / C::BKD;
-  P.num_tiles = P.m_pairs * P.n_tiles;
-  P.group_m = group_m_env(8);
-  P.c_f32 = p.c_f32;
-  P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
-  P.ldc = p.ldc;
-  P.alpha = p.alpha;
-  P.idesc_ab = p.idesc_ab;
-  P.bias = p.bias;
-  P.act = p.act;
-  P.gate_from_c = p.gate_from_c;
-  P.peers = p.peers;
-  P.vec_f32 = p.c_f32 == nullptr                            ? 0
-              : (aligned32(p.c_f32) && (p.ldc % 8) == 0)    ? 2
-              : (aligned16(p.c_f32) && (p.ldc % 4) == 0)    ? 1
-                                                            : 0;
-  P.vec_bf16 = p.c_bf16 == nullptr                          ? 0
-               : (aligned32(p.c_bf16) && (p.ldc % 16) == 0) ? 2
-               : (aligned16(p.c_bf16) && (p.ldc % 8) == 0)  ? 1
-                                                            : 0;
-  P.status = p.status;
-  P.timeout_ns = p.timeout_ns;
-  P.stall_producer = p.stall_producer;
+  const sp24::PairParams P = pair_params(p, C::BKD, 256, 256);
   const int pairs = std::max(1, std::min(P.num_tiles, di.sm_count / 2));
   kern<<<2 * pairs, sp24::kPairThreads, C::SMEM_BYTES, stream>>>(ta, tb, te, P);
   SP24_CUDA_TRY(cudaGetLastError());
@@ -486,6 +495,17 @@ int splitk_units(int bn) {
 }
 
 using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t);
+
+// Pair-kernel variant: the 256 x 256 tile with coarse stages, or its
+// fine-staged form (SP24_PAIR_FINE=1).
+template <int DT>
+LaunchFn pick_pair_dt() {
+  return pair_fine_stages() ? launch_gemm2sm<DT, 1> : launch_gemm2sm<DT, 0>;
+}
+
+LaunchFn pick_pair(sp24_dtype dt) {
+  return dt == SP24_F16 ? pick_pair_dt<0>() : dt == SP24_BF16 ? pick_pair_dt<1>() : pick_pair_dt<2>();
+}
 
 template <int DT>
 LaunchFn pick_splitk(int bn, int kb) {
@@ -743,11 +763,7 @@ sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const Devic
                          cudaStream_t stream) {
   const DeviceInfo* di = &di_ref;
   if (use_pair_kernel(d->m, d->n, d->tile_n)) {
-    const bool fine = pair_fine_stages();
-    LaunchFn pf = d->dtype == SP24_F16    ? (fine ? launch_gemm2sm<0, 1> : launch_gemm2sm<0, 0>)
-                  : d->dtype == SP24_BF16 ? (fine ? launch_gemm2sm<1, 1> : launch_gemm2sm<1, 0>)
-                                          : (fine ? launch_gemm2sm<2, 1> : launch_gemm2sm<2, 0>);
-    return pf(p, *di, stream);
+    return pick_pair(d->dtype)(p, *di, stream);
   }
   const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);
   if (use_splitk_kernel(d->m, d->n, bn, di->sm_count)) {
