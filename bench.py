@@ -248,10 +248,65 @@ def cpu_reference_rate(cfg, seconds=10.0, threads=None):
         f"{t:.1f} s")
 
 
+def reference_gpu_legacy(args, cfg):
+    """The reference's only kernels that run on sm_100: its legacy warp-level
+    mma.sp.sync GEMMs (mma_sp_m16n8k32_fp32{fp16,bf16}.cu, built for sm_100a
+    from the reference sources by oracle/Makefile), timed on this GPU over the
+    same workload with CUDA events.  Inputs are made on the device (sp24's
+    compression, bit-exact with the reference's; the k32 kernels read the
+    reference's row-major metadata bytes as words); the timed launches are the
+    reference's kernel alone, fp32 output only.  None when the config has no
+    such kernel (e4m3) or its shape does not tile by 64."""
+    import oracle
+    if cfg["dt"] not in (0, 1) or not oracle.ref_legacy_available():
+        return None
+    m, n, k = cfg["m"], cfg["n"], cfg["k"]
+    if m % 64 or n % 64 or k % 32:
+        return None
+    import torch
+    import sp24
+    if not torch.cuda.is_available():
+        return None
+    which = 2 if cfg["dt"] == 0 else 3
+    ac, meta, img, b, _ = make_inputs(cfg, 0, torch, sp24)
+    del img
+    c = torch.empty((m, n), device=ac.device)
+    stream = torch.cuda.current_stream()
+
+    def launch():
+        rc = oracle.ref_legacy_launch(which, ac.data_ptr(), b.data_ptr(), c.data_ptr(),
+                                      meta.data_ptr(), m, n, k, stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"reference legacy kernel launch failed: {rc}")
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    steps = 10
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        launch()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    name = oracle.LEGACY_FILES[which].replace(".cu", "_kernel")
+    return {"kernel": f"{name}<LOAD_METHOD 2> (reference source, mma.sp.sync, sm_100a build)",
+            "value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms, "steps": steps, "warmup": 3, "output": "fp32",
+            "timing": "CUDA events on the launching stream, inputs resident"}
+
+
 def run_reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    gpu_legacy = None
+    if args.gpus == 1:
+        try:
+            gpu_legacy = reference_gpu_legacy(args, cfg)
+        except Exception as exc:   # reported, not fatal: the arm's value is the CPU path
+            gpu_legacy = {"unavailable": f"{type(exc).__name__}: {exc}"}
     steps = []
     info = None
     for _ in range(max(1, args.warmup_ref)):
@@ -277,6 +332,8 @@ def run_reference_arm(args, cfg):
         "note": "reference's CPU path (its sm_90a kernels cannot run on sm_100); ms_per_step is "
                 "the full-problem time at the sampled rate",
     }
+    if gpu_legacy is not None:
+        line["gpu_legacy"] = gpu_legacy
     print(json.dumps(line), flush=True)
 
 

@@ -135,13 +135,34 @@ def ref_legacy_available() -> bool:
     return os.path.exists(REF_LEGACY_LIB)
 
 
+_rl = None
+
+
+def _ref_legacy_lib():
+    global _rl
+    if _rl is None:
+        r = ctypes.CDLL(REF_LEGACY_LIB)
+        r.ref_legacy_case.restype = c_int
+        r.ref_legacy_case.argtypes = [c_int, c_int, c_int, c_int] + [c_void_p] * 5
+        r.ref_legacy_launch.restype = c_int
+        r.ref_legacy_launch.argtypes = [c_int] + [c_void_p] * 4 + [c_int] * 3 + [c_void_p]
+        _rl = r
+    return _rl
+
+
+def ref_legacy_launch(which: int, a_c: int, b: int, c: int, e: int, m: int, n: int, k: int,
+                      stream: int = 0) -> int:
+    """Launches the reference's own kernel of legacy main `which` (its
+    mma.sp.sync kernel, built for sm_100a) on device pointers in that main's
+    formats; returns the launch's CUDA error code (0 = launched)."""
+    return _ref_legacy_lib().ref_legacy_launch(which, a_c, b, c, e, m, n, k, stream)
+
+
 def ref_legacy_case(which: int, m: int, n: int, k: int, with_c: bool = True):
     """A legacy main replayed by the reference's own host code at m x n x k:
     (a, b, a_c, meta words, c or None); meta is [k/16][m/2] words for the
     m16n8k16 mains and [m][k/32] for the m16n8k32 ones."""
-    r = ctypes.CDLL(REF_LEGACY_LIB)
-    r.ref_legacy_case.restype = c_int
-    r.ref_legacy_case.argtypes = [c_int, c_int, c_int, c_int] + [c_void_p] * 5
+    r = _ref_legacy_lib()
     a = np.empty((m, k), np.uint16)
     b = np.empty((k, n), np.uint16)
     ac = np.empty((m, k // 2), np.uint16)

@@ -10,8 +10,16 @@
 // for the m16n8k16 files the main's per-16-column-strip compression with the
 // strips' metadata concatenated (:277-297 of the fp16 file).  C is the fp32
 // sequential CPU product the mains verify against (their inline loops).  The
-// files' kernels are compiled for sm_90 and never launched; their main()s are
-// renamed away.
+// main()s are renamed away.
+//
+// ref_legacy_launch runs the files' own kernels (warp-level mma.sp, which
+// sm_100a still executes) the way their mains launch them: the LOAD_METHOD
+// the main picks, grid (N/64, M/64), 256 threads.  Dynamic shared memory is
+// 32 KB for all four.  The m16n8k32 fp16 main passes 6272 B (:457-458), less
+// than its kernel's own footprint of 6400 B (A 2 KB + B 4 KB + 64 metadata
+// words, :317-320), so this launcher does not copy that value.  Every global
+// access of these kernels is bounds-checked against M, N and K
+// (e.g. mma_sp_m16n8k32_fp32bf16.cu:258-276, 308-316).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -156,6 +164,46 @@ int ref_legacy_case(int which, int m, int n, int k, void* a, void* b, void* ac, 
                     m, n, k);
   }
   return 0;
+}
+
+// Launches the reference kernel of legacy main `which` on `stream` over
+// device buffers in that main's formats: a_c M x K/2, b K x N, e as
+// ref_legacy_case describes, c M x N fp32 (all row-major, dense pitches).
+// Returns the launch's cudaError_t, or -1 for a shape the kernels do not
+// tile (M and N multiples of 64, K of 32).
+int ref_legacy_launch(int which, const void* a_c, const void* b, float* c, const uint32_t* e,
+                      int m, int n, int k, void* stream) {
+  if (m <= 0 || n <= 0 || k <= 0 || m % 64 || n % 64 || k % 32) return -1;
+  const dim3 grid(n / 64, m / 64), block(256);
+  const int smem = 32768;
+  // The mains' LOAD_METHOD_MANUAL (k16) and LOAD_METHOD_MANUAL_LANE (k32)
+  // are both 2 (their macros are undefined again above).
+  constexpr int kManual = 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (which) {
+    case 0:
+      k16_f16::mma_sp_m16n8k16_fp32fp16_kernel<kManual><<<grid, block, smem, s>>>(
+          static_cast<const half*>(a_c), static_cast<const half*>(b), c, e, m, n, k);
+      break;
+    case 1:
+      k16_bf16::mma_sp_m16n8k16_fp32bf16_kernel<kManual>
+          <<<grid, block, smem, s>>>(static_cast<const __nv_bfloat16*>(a_c),
+                                     static_cast<const __nv_bfloat16*>(b), c, e, m, n, k);
+      break;
+    case 2:
+      k32_f16::mma_sp_m16n8k32_fp32fp16_kernel<kManual>
+          <<<grid, block, smem, s>>>(static_cast<const half*>(a_c), static_cast<const half*>(b),
+                                     c, e, m, n, k);
+      break;
+    case 3:
+      k32_bf16::mma_sp_m16n8k32_fp32bf16_kernel<kManual>
+          <<<grid, block, smem, s>>>(static_cast<const __nv_bfloat16*>(a_c),
+                                     static_cast<const __nv_bfloat16*>(b), c, e, m, n, k);
+      break;
+    default:
+      return -1;
+  }
+  return static_cast<int>(cudaGetLastError());
 }
 
 }  // extern "C"

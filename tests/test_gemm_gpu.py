@@ -385,6 +385,35 @@ def test_legacy_entry_points_full_size(which):
     assert err <= 1e-2, err
 
 
+@pytest.mark.parametrize("which", [0, 1, 2, 3])
+def test_reference_legacy_kernels_on_this_gpu(which):
+    """The reference's own legacy kernels (mma_sp_m16n8k{16,32}_fp32{fp16,bf16}
+    .cu, built for sm_100a by oracle/Makefile) run on this GPU over the
+    inputs their main generates, in their own A_c / metadata formats; sp24_gemm
+    takes the same device buffers (m16n8k16 words as SP24_META_K16, m16n8k32
+    words as SP24_META_REF).  Both meet the main's rule against its CPU
+    product, and sp24 matches the reference kernel within 1e-3 of the
+    largest |C| (the two tensor-core paths sum K in different orders)."""
+    if not oracle.ref_legacy_available():
+        pytest.skip("reference legacy library not built")
+    m, n, k = 512, 384, 1024
+    dt = oracle.legacy_dtype(which)
+    a, b, ac, e, c_cpu = oracle.ref_legacy_case(which, m, n, k)
+    ac_t, b_t = to_dev(ac, dt), to_dev(b, dt)
+    e_t = torch.from_numpy(e.view(np.int32).copy()).to(DEV)
+    c_ref = torch.full((m, n), float("nan"), device=DEV)
+    rc = oracle.ref_legacy_launch(which, ac_t.data_ptr(), b_t.data_ptr(), c_ref.data_ptr(),
+                                  e_t.data_ptr(), m, n, k, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    fmt = sp24.META_K16 if which < 2 else sp24.META_REF
+    c, _ = sp24.gemm(ac_t, e_t, b_t, m, n, k, meta_format=fmt, dtype=lib_dtype(dt))
+    torch.cuda.synchronize()
+    assert np.abs(c_ref.cpu().numpy() - c_cpu).max() <= 0.1
+    assert np.abs(c.cpu().numpy() - c_cpu).max() <= 0.1
+    scale = c_ref.abs().max().item() + 1.0
+    assert (c - c_ref).abs().max().item() <= 1e-3 * scale
+
+
 # ------------------------------------------------------------------ mixed fp8
 def test_legacy_fp8_suite_on_gpu(golden):
     """Every case of the reference's mixed fp8 entry point
