@@ -106,7 +106,6 @@ struct PairCfg {
   static constexpr uint32_t IDESC = make_idesc_sparse(FMT, 256, 256, true);
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
-  static_assert(MMAS == 4 || MMAS == 2, "full stages are issued as one block of MMAs");
   static_assert(LOADS <= 32, "one lane per TMA box");
 };
 
@@ -370,7 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     // The whole warp runs this loop converged (all operands warp-uniform);
-    // tcgen05 instructions are issued by one elected lane inside the asm.
+    // one elected lane issues each stage's tcgen05 ops.
     // Descriptors are formed once; per stage only the start-address field
     // moves (stage offset >> 4 added to the 64-bit descriptor), per MMA by a
     // compile-time step.  Metadata: atom a of a stage lives in TMEM columns
@@ -384,7 +383,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const uint64_t edesc0 =
           make_sdesc(smem_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
       constexpr uint32_t SD = C::STAGE_BYTES >> 4;
-      constexpr int kPerAtom = 128 / C::MMA_K;
       // Per-MMA constants, per position `sub` of the stage inside its atom
       // group: metadata column offset and sparsity selector.
       uint32_t ecol[C::SPA][C::MMAS], isel[C::SPA][C::MMAS];
@@ -399,7 +397,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           ecol[sb][j] = 4u * static_cast<uint32_t>(koff / 128) + (col & ~1u);
           isel[sb][j] = C::IDESC | P.idesc_ab | (col & 1u);
         }
-      (void)kPerAtom;
       int s = 0;
       uint32_t ph = 0, soff = 0, aph = 0, ebuf = 0;
       bool ok = true, any = false;
@@ -421,48 +418,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           const int sub = ks % C::SPA;
           if (sub == 0) ebuf ^= static_cast<uint32_t>(C::E_PER * 4);
           const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
-          if (sub == 0) {
-#pragma unroll
-            for (int a = 0; a < C::E_PER; ++a)
-              tc_cp_elect<2>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
-          }
           const int kleft = P.k - ks * C::BKD;
           const uint32_t acc0 = ks > 0 ? 1u : 0u;
-          uint64_t ad[C::MMAS], bd[C::MMAS];
-          uint32_t ed[C::MMAS], id[C::MMAS];
+          if (elect_one()) {
+            if (sub == 0) {
 #pragma unroll
-          for (int j = 0; j < C::MMAS; ++j) {
-            ad[j] = adesc0 + soff + j * 2;
-            bd[j] = bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4);
-            ed[j] = e_tmem + (C::SPA == 1 ? ecol[0][j] : ecol[sub & (C::SPA - 1)][j]);
-            id[j] = C::SPA == 1 ? isel[0][j] : isel[sub & (C::SPA - 1)][j];
-          }
-          if (kleft >= C::BKD) {
-            if constexpr (C::MMAS == 4) {
-              tc_mma_sp_elect_x4<2, C::KIND>(tmem_base, ad, bd, ed, id, acc0);
-            } else {
-              tc_mma_sp_elect_x2<2, C::KIND>(tmem_base, ad[0], bd[0], ed[0], id[0], ad[1], bd[1],
-                                             ed[1], id[1], acc0);
+              for (int a = 0; a < C::E_PER; ++a)
+                tc_cp<2>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
             }
-          } else {
 #pragma unroll
             for (int j = 0; j < C::MMAS; ++j)
               if (j * C::MMA_K < kleft)
-                tc_mma_sp_elect<2, C::KIND>(tmem_base, ad[j], bd[j], ed[j], id[j],
-                                            j > 0 ? 1u : acc0);
+                tc_mma<2, C::KIND>(tmem_base, adesc0 + soff + j * 2,
+                                   bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4),
+                                   e_tmem + (C::SPA == 1 ? ecol[0][j] : ecol[sub & (C::SPA - 1)][j]),
+                                   C::SPA == 1 ? isel[0][j] : isel[sub & (C::SPA - 1)][j],
+                                   j > 0 ? 1u : acc0);
+            tc_commit_to<2>(&empty_bar[s], static_cast<uint16_t>(3));
           }
+          __syncwarp();
           any = true;
-          tc_commit_elect<2>(&empty_bar[s], static_cast<uint16_t>(3));
           soff += SD;
           if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
         if (!ok) break;
-        tc_commit_elect<2>(&accf_bar, static_cast<uint16_t>(3));
+        if (elect_one()) tc_commit_to<2>(&accf_bar, static_cast<uint16_t>(3));
+        __syncwarp();
         aph ^= 1u;
       }
       if (!ok && any) {
         volatile int dummy = 0;
-        tc_commit_elect<2>(&drain_bar, static_cast<uint16_t>(1));
+        if (elect_one()) tc_commit_to<2>(&drain_bar, static_cast<uint16_t>(1));
+        __syncwarp();
         if (lane == 0) mbar_wait(&drain_bar, 0, &dummy, tmo);
         __syncwarp();
       }

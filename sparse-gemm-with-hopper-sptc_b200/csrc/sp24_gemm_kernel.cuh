@@ -134,7 +134,7 @@ struct GemmCfg {
   static_assert(BN % B_BOXN == 0, "B tile must be whole TMA boxes");
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
-  static_assert(MMAS == 2, "a full stage is issued as one block of two MMAs");
+  static_assert(MMAS == 2, "two MMAs per stage (metadata column arithmetic)");
 };
 
 SP24_DEV void tile_coords(const GemmParams& P, int t, int& mb, int& nb) {
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Converged warp loop; tcgen05 instructions issued by an elected lane.
+    // Converged warp loop; one elected lane issues each stage's tcgen05 ops.
     {
       const uint32_t a_base = smem_u32(smem);
       const uint64_t adesc0 = make_sdesc(a_base, 16, 512, kLayoutSW64);
@@ -376,45 +376,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int sub = ks % C::STAGES_PER_ATOM;
           const uint32_t e_tmem =
               tmem_base + static_cast<uint32_t>(C::E_COL + ((ks / C::STAGES_PER_ATOM) & 1) * 4);
-          // Metadata atom: 128 rows of 16 B, rows contiguous -> K-major
-          // no-swizzle canonical layout, 8-row groups 128 B apart.
-          if (sub == 0) tc_cp_elect<1>(e_tmem, edesc0 + soff);
           // Metadata column of MMA j inside the atom: kind::f16 uses one
           // 32-bit column per K=32 MMA, kind::f8f6f4 two per K=64 MMA.  The
           // operand address is even; the odd column is picked through the
           // sparsity selector (instruction descriptor bits 0-1).
-          uint32_t ecol[C::MMAS], isel[C::MMAS];
-          uint64_t ad[C::MMAS], bd[C::MMAS];
-#pragma unroll
-          for (int j = 0; j < C::MMAS; ++j) {
-            const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(sub * C::MMAS + j)
-                                                : static_cast<uint32_t>(2 * j);
-            ecol[j] = e_tmem + (col & ~1u);
-            isel[j] = C::IDESC | P.idesc_ab | (col & 1u);
-            ad[j] = adesc0 + soff + j * 2;
-            bd[j] = bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4);
-          }
           const int kleft = P.k - ks * C::BKD;
           const uint32_t acc0 = ks > 0 ? 1u : 0u;
-          if (kleft >= C::BKD) {
-            tc_mma_sp_elect_x2<1, C::KIND>(d_tmem, ad[0], bd[0], ecol[0], isel[0], ad[1], bd[1],
-                                           ecol[1], isel[1], acc0);
-          } else {
-            tc_mma_sp_elect<1, C::KIND>(d_tmem, ad[0], bd[0], ecol[0], isel[0], acc0);
+          if (elect_one()) {
+            // Metadata atom: 128 rows of 16 B, rows contiguous -> K-major
+            // no-swizzle canonical layout, 8-row groups 128 B apart.
+            if (sub == 0) tc_cp<1>(e_tmem, edesc0 + soff);
+#pragma unroll
+            for (int j = 0; j < C::MMAS; ++j) {
+              const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>(sub * C::MMAS + j)
+                                                  : static_cast<uint32_t>(2 * j);
+              if (j * C::MMA_K < kleft)
+                tc_mma<1, C::KIND>(d_tmem, adesc0 + soff + j * 2,
+                                   bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4),
+                                   e_tmem + (col & ~1u), C::IDESC | P.idesc_ab | (col & 1u),
+                                   j > 0 ? 1u : acc0);
+            }
+            tc_commit_to<1>(&empty_bar[s], 0);
           }
+          __syncwarp();
           any_issued = true;
-          tc_commit_elect<1>(&empty_bar[s], 0);
           soff += SD;
           if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
         if (!ok) break;
-        tc_commit_elect<1>(&accf_bar[ab], 0);
+        if (elect_one()) tc_commit_to<1>(&accf_bar[ab], 0);
+        __syncwarp();
         if (++ab == C::ACC) ab = 0, aph ^= 1u;
       }
       if (!ok && any_issued) {
         // Error path: wait for MMAs in flight before TMEM is released.
         volatile int dummy_abort = 0;
-        tc_commit_elect<1>(&drain_bar, 0);
+        if (elect_one()) tc_commit_to<1>(&drain_bar, 0);
+        __syncwarp();
         if (lane == 0) mbar_wait(&drain_bar, 0, &dummy_abort, tmo);
         __syncwarp();
       }

@@ -341,40 +341,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       ebuf ^= static_cast<uint32_t>(G * C::E_S * 4);
       const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
-#pragma unroll
-      for (int a = 0; a < G * C::E_S; ++a)
-        if (g * C::E_S + a % C::E_S < P.katoms)
-          tc_cp_elect<1>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
       const int kleft = P.k - g * C::BKD;
+      if (elect_one()) {
 #pragma unroll
-      for (int w = 0; w < G; ++w)
+        for (int a = 0; a < G * C::E_S; ++a)
+          if (g * C::E_S + a % C::E_S < P.katoms)
+            tc_cp<1>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
 #pragma unroll
-        for (int u = 0; u < KB; ++u)
+        for (int w = 0; w < G; ++w)
 #pragma unroll
-          for (int j = 0; j < C::MMAS_U; ++j) {
-            const int kk = u * C::UK + j * C::MMA_K;   // dense K inside the stage
-            if (kk < kleft) {
-              const int atom_in = w * C::E_S + kk / 128;
-              const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>((kk % 128) / 32)
-                                                  : static_cast<uint32_t>(2 * ((kk % 128) / 64));
-              const uint64_t ad = adesc0 + soff + (w * KB + u) * (C::A_BOX >> 4) + j * 2;
-              const uint64_t bd =
-                  bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4);
-              tc_mma_sp_elect<1, C::KIND>(tmem_base + static_cast<uint32_t>(w * BN), ad, bd,
-                                          e_tmem + 4 * atom_in + (col & ~1u),
-                                          C::IDESC | P.idesc_ab | (col & 1u),
-                                          (i > 0 || kk > 0) ? 1u : 0u);
+          for (int u = 0; u < KB; ++u)
+#pragma unroll
+            for (int j = 0; j < C::MMAS_U; ++j) {
+              const int kk = u * C::UK + j * C::MMA_K;   // dense K inside the stage
+              if (kk < kleft) {
+                const int atom_in = w * C::E_S + kk / 128;
+                const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>((kk % 128) / 32)
+                                                    : static_cast<uint32_t>(2 * ((kk % 128) / 64));
+                tc_mma<1, C::KIND>(
+                    tmem_base + static_cast<uint32_t>(w * BN),
+                    adesc0 + soff + (w * KB + u) * (C::A_BOX >> 4) + j * 2,
+                    bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4),
+                    e_tmem + 4 * atom_in + (col & ~1u), C::IDESC | P.idesc_ab | (col & 1u),
+                    (i > 0 || kk > 0) ? 1u : 0u);
+              }
             }
-          }
+        tc_commit_to<1>(&empty_bar[s], 0);
+      }
+      __syncwarp();
       any = true;
-      tc_commit_elect<1>(&empty_bar[s], 0);
       soff += SD;
       if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
     }
-    if (ok) tc_commit_elect<1>(&accf_bar, 0);
+    if (ok && elect_one()) tc_commit_to<1>(&accf_bar, 0);
+    __syncwarp();
     if (!ok && any) {
       volatile int dummy = 0;
-      tc_commit_elect<1>(&drain_bar, 0);
+      if (elect_one()) tc_commit_to<1>(&drain_bar, 0);
+      __syncwarp();
       if (lane == 0) mbar_wait(&drain_bar, 0, &dummy, tmo);
       __syncwarp();
     }
@@ -407,13 +411,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int w = 0; w < G; ++w) tmem_ld_wait(r[w]);
         if (S == 1) {
+          // Finished values of this lane's row go to the warp's rows of the
+          // idle ring; the warp then stores them row by row (below).
           float v[C::CH];
 #pragma unroll
           for (int e = 0; e < C::CH; ++e)
             v[e] = split_out<G>(P, __uint_as_float(r[0][e]), __uint_as_float(r[G - 1][e]), bg,
                                 bu);
           if (P.gate_from_c && live) gate_mul_row<C::CH>(P, v, row, nb * BN + c);
-          store_values<C::CH>(P, v, row, nb * BN + c);
+#pragma unroll
+          for (int e = 0; e < C::CH; e += 4)
+            *reinterpret_cast<float4*>(red + row_l * C::RS + c + e) =
+                make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
         } else {
 #pragma unroll
           for (int w = 0; w < G; ++w)
@@ -422,6 +431,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               *reinterpret_cast<float4*>(red + (w * kBlockM + row_l) * C::RS + c + v) =
                   make_float4(__uint_as_float(r[w][v]), __uint_as_float(r[w][v + 1]),
                               __uint_as_float(r[w][v + 2]), __uint_as_float(r[w][v + 3]));
+        }
+      }
+      if (S == 1) {
+        // Coalesced stores: the warp's 32 rows leave as contiguous row
+        // segments (BN / 4 lanes per row, 16 B each), instead of one 16 B
+        // piece of 32 different rows per store instruction.
+        __syncwarp();
+        constexpr int NV = BN / 4;
+        for (int idx = lane; idx < 32 * NV; idx += 32) {
+          const int rl = q * 32 + idx / NV;
+          const int cg = idx - (idx / NV) * NV;
+          const float4 o = *reinterpret_cast<const float4*>(red + rl * C::RS + cg * 4);
+          store_vec4(P, o, mb * kBlockM + rl, nb * BN + cg * 4);
         }
       }
     }

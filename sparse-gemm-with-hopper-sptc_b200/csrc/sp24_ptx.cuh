@@ -334,110 +334,53 @@ SP24_DEV void tc_mma_sp_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, ui
   }
 }
 
-// ---------------------------------------------------------------- warp-converged issue
-// The MMA-issuing warp runs its loop with all 32 lanes converged, so every
-// operand below is warp-uniform; inside the asm one lane is elected to issue.
-// A same-box A/B run measured no throughput difference between this form and
-// lane-0-only code with one asm block per MMA; the converged form keeps the
-// issuing warp free of divergent branches around each tcgen05 instruction.
-template <int CG>
-SP24_DEV void tc_cp_elect(uint32_t taddr, uint64_t sdesc) {
-  if constexpr (CG == 1) {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "@e tcgen05.cp.cta_group::1.128x128b [%0], %1;\n\t}\n" ::"r"(taddr),
-        "l"(sdesc)
-        : "memory");
-  } else {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "@e tcgen05.cp.cta_group::2.128x128b [%0], %1;\n\t}\n" ::"r"(taddr),
-        "l"(sdesc)
-        : "memory");
-  }
+// ---------------------------------------------------------------- stage issue
+// The MMA-issuing warp runs its loop converged (every operand warp-uniform)
+// and elects ONE lane per stage, which then issues the stage's tcgen05.cp,
+// MMAs and commit as plain instructions:
+//
+//   if (elect_one()) { tc_cp<CG>(...); tc_mma<CG, KIND>(...); ...; tc_commit<CG>(...); }
+//   __syncwarp();
+//
+// Measured on B200 in the narrow-N kernel (%globaltimer stamps): a separate
+// elect.sync around every instruction costs ~56 ns per MMA, four MMAs per
+// elected asm block ~24 ns each, one election per stage ~20 ns each.  With
+// skinny tiles (8 MMAs per 44 KB stage) the per-instruction form made the
+// issuing warp, not HBM, the limit.  The same lane is elected every time
+// (the lowest active lane), so its commits track all the MMAs it issued.
+
+// True in exactly one lane of the converged warp.
+SP24_DEV bool elect_one() {
+  uint32_t p;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}\n"
+      : "=r"(p));
+  return p != 0;
 }
 
 template <int CG>
-SP24_DEV void tc_commit_elect(uint64_t* bar, uint16_t mask) {
+SP24_DEV void tc_cp(uint32_t taddr, uint64_t sdesc) {
+  if constexpr (CG == 1) tc_cp_128x128b(taddr, sdesc);
+  else tc_cp_128x128b_pair(taddr, sdesc);
+}
+
+template <int CG, int KIND>
+SP24_DEV void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t e, uint32_t idesc, uint32_t acc) {
+  if constexpr (CG == 1) tc_mma_sp<KIND>(d, a, b, e, idesc, acc);
+  else tc_mma_sp_pair<KIND>(d, a, b, e, idesc, acc);
+}
+
+// CG 1: arrive on this CTA's barrier; CG 2: on the barrier at the same offset
+// in every CTA of `mask`.
+template <int CG>
+SP24_DEV void tc_commit_to(uint64_t* bar, uint16_t mask) {
   if constexpr (CG == 1) {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
-            smem_u32(bar))
-        : "memory");
+    tc_commit(bar);
     (void)mask;
   } else {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;\n\t}\n" ::"r"(smem_u32(bar)),
-        "h"(mask)
-        : "memory");
+    tc_commit_pair(bar, mask);
   }
 }
-
-#define SP24_MMA_SP_STR(CG, KIND)                                                             \
-  "tcgen05.mma.sp.cta_group::" #CG ".kind::" #KIND
-
-// One sparse MMA, elected lane.
-template <int CG, int KIND>
-SP24_DEV void tc_mma_sp_elect(uint32_t d, uint64_t a, uint64_t b, uint32_t e, uint32_t idesc,
-                              uint32_t acc) {
-#define SP24_ONE(CGS, KS)                                                                       \
-  asm volatile("{\n\t.reg .pred e, p;\n\telect.sync _|e, 0xffffffff;\n\t"                      \
-               "setp.ne.b32 p, %5, 0;\n\t"                                                    \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %1, %2, [%3], %4, p;\n\t}\n" ::"r"(d),    \
-               "l"(a), "l"(b), "r"(e), "r"(idesc), "r"(acc)                                    \
-               : "memory")
-  if constexpr (CG == 1 && KIND == 0) SP24_ONE(1, f16);
-  else if constexpr (CG == 1) SP24_ONE(1, f8f6f4);
-  else if constexpr (KIND == 0) SP24_ONE(2, f16);
-  else SP24_ONE(2, f8f6f4);
-#undef SP24_ONE
-}
-
-// Two sparse MMAs into the same accumulator from one asm block; the second
-// always accumulates.
-template <int CG, int KIND>
-SP24_DEV void tc_mma_sp_elect_x2(uint32_t d, uint64_t a0, uint64_t b0, uint32_t e0, uint32_t i0,
-                                 uint64_t a1, uint64_t b1, uint32_t e1, uint32_t i1,
-                                 uint32_t acc) {
-#define SP24_TWO(CGS, KS)                                                                       \
-  asm volatile("{\n\t.reg .pred e, p;\n\telect.sync _|e, 0xffffffff;\n\t"                      \
-               "setp.ne.b32 p, %9, 0;\n\t"                                                    \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %1, %2, [%3], %4, p;\n\t"                 \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %5, %6, [%7], %8, 1;\n\t}\n" ::"r"(d),    \
-               "l"(a0), "l"(b0), "r"(e0), "r"(i0), "l"(a1), "l"(b1), "r"(e1), "r"(i1), "r"(acc) \
-               : "memory")
-  if constexpr (CG == 1 && KIND == 0) SP24_TWO(1, f16);
-  else if constexpr (CG == 1) SP24_TWO(1, f8f6f4);
-  else if constexpr (KIND == 0) SP24_TWO(2, f16);
-  else SP24_TWO(2, f8f6f4);
-#undef SP24_TWO
-}
-
-// Four sparse MMAs into the same accumulator from one asm block.
-template <int CG, int KIND>
-SP24_DEV void tc_mma_sp_elect_x4(uint32_t d, const uint64_t (&a)[4], const uint64_t (&b)[4],
-                                 const uint32_t (&e)[4], const uint32_t (&i)[4], uint32_t acc) {
-#define SP24_FOUR(CGS, KS)                                                                      \
-  asm volatile("{\n\t.reg .pred e, p;\n\telect.sync _|e, 0xffffffff;\n\t"                      \
-               "setp.ne.b32 p, %17, 0;\n\t"                                                   \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %1, %2, [%3], %4, p;\n\t"                 \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %5, %6, [%7], %8, 1;\n\t"                 \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %9, %10, [%11], %12, 1;\n\t"              \
-               "@e " SP24_MMA_SP_STR(CGS, KS) " [%0], %13, %14, [%15], %16, 1;\n\t}\n" ::"r"(d),\
-               "l"(a[0]), "l"(b[0]), "r"(e[0]), "r"(i[0]), "l"(a[1]), "l"(b[1]), "r"(e[1]),     \
-               "r"(i[1]), "l"(a[2]), "l"(b[2]), "r"(e[2]), "r"(i[2]), "l"(a[3]), "l"(b[3]),     \
-               "r"(e[3]), "r"(i[3]), "r"(acc)                                                  \
-               : "memory")
-  if constexpr (CG == 1 && KIND == 0) SP24_FOUR(1, f16);
-  else if constexpr (CG == 1) SP24_FOUR(1, f8f6f4);
-  else if constexpr (KIND == 0) SP24_FOUR(2, f16);
-  else SP24_FOUR(2, f8f6f4);
-#undef SP24_FOUR
-}
-#undef SP24_MMA_SP_STR
 
 // Lane 0 runs the bounded wait; the verdict is broadcast so the warp stays
 // converged.
