@@ -12,11 +12,14 @@ dense-equivalent FLOPs of all ranks / max-over-ranks time.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sp24|reference]
                     [--config 2|3|4|5] [--allgather [nccl|fused|both]]
                     [--config 4 --layer up|down --tokens 8|16|64|128|4096]
+                    [--l2 rotate|clean]
 
 Configuration 4 (the MLP layers) at T <= 128 tokens is bound by HBM: its
 roofline is reported in GB/s of algorithmic bytes against the measured copy
-bandwidth, and because its operands fit in L2, L2 is cleaned before every
-step and each step is timed alone.
+bandwidth.  Its operands fit in L2, so the steps rotate over enough copies of
+the weights to exceed twice the L2 and run back to back, as the layers of a
+decode pass do (--l2 clean instead cleans L2 before every step and times each
+step alone).
 
 Metric: dense-equivalent TFLOP/s (2MNK/t).  `roofline` compares the kernel
 with the sparse tensor peak derived from the measured dense bf16 peak
@@ -128,6 +131,21 @@ class ClockSampler:
                  "-i", self.gpus, "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # nvidia-smi takes a while to start: hold the timed region until its
+        # first sample is written, so short regions are sampled too.
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            self.f.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
+        self.skip = 0
+        try:
+            with open(self.path) as fh:
+                self.skip = sum(1 for _ in fh)   # samples taken before the region
+        except OSError:
+            pass
         return self
 
     def __exit__(self, *exc):
@@ -144,7 +162,10 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
+        lines = open(self.path).read().splitlines()
+        if len(lines) > getattr(self, "skip", 0):
+            lines = lines[getattr(self, "skip", 0):]
+        for line in lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -359,6 +380,12 @@ def main():
     ap.add_argument("--gated", action="store_true",
                     help="configuration 4, W_up/W_gate: one fused SwiGLU launch "
                          "(silu(W_gate B) * W_up B) per step instead of one GEMM")
+    ap.add_argument("--l2", default="rotate", choices=["rotate", "clean"],
+                    help="workloads that fit in L2: rotate over weight copies that exceed it "
+                         "(default), or clean L2 before every step and time each step alone")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="rotating (L2-sized) workloads: launch every step from Python instead "
+                         "of replaying CUDA graphs of the same launches")
     ap.add_argument("--steps-ref", type=int, default=1)
     ap.add_argument("--warmup-ref", type=int, default=1)
     args = ap.parse_args()
@@ -405,27 +432,41 @@ def main():
         epi.a_c_up, epi.lda_c_up = ac_up.data_ptr(), ac_up.stride(0)
         epi.meta_up, epi.alpha_up = img_up.data_ptr(), 1.0
 
-    def step():
-        if gemms == 2:
-            rc = lib.sp24_gemm_fused(ctypes.byref(desc), ctypes.byref(epi), sptr)
-        else:
-            rc = lib.sp24_gemm(ctypes.byref(desc), sptr)
-        if rc != 0:
-            raise sp24.Sp24Error(rc, "sp24_gemm")
-
     def barrier():
         if world > 1:
             dist.barrier()
 
     # Inputs and outputs that fit in L2 twice over would be served from L2 on
-    # back-to-back steps; then every step starts from a cleaned L2: a 256 MB
-    # write (evicts everything) followed by a read of the same buffer (leaves
-    # L2 holding clean lines, so the GEMM's own reads pay no write-backs),
-    # and each step is timed alone with its own events.
+    # back-to-back steps.  Two ways to keep every step's weight reads in HBM:
+    #   rotate (default): as many copies of the weights (A_c + metadata image)
+    #     as exceed twice the L2, step i using copy i % copies, all steps back
+    #     to back between one pair of events -- a decode pass streaming one
+    #     layer's weights after another's;
+    #   clean: before every step a 256 MB write (evicts everything) and a read
+    #     of the same buffer (leaves clean lines, so the GEMM pays no
+    #     write-backs), each step timed alone with its own events; that time
+    #     includes the launch latency after the cleaning kernels.
     esz = 1 if dt == 2 else 2
     out_bytes = sum(4 if o == "f32" else 2 for o in cfg["out"]) * m * n
     in_bytes = gemms * (m * k // 2 * esz + m * k // 8) + k * n * esz
-    flush_l2 = in_bytes + out_bytes < 2 * L2_BYTES
+    fits_l2 = in_bytes + out_bytes < 2 * L2_BYTES
+    flush_l2 = fits_l2 and args.l2 == "clean"
+    weight_bytes = gemms * (m * k // 2 * esz + m * k // 8)
+    copies = (2 * L2_BYTES) // weight_bytes + 2 if (fits_l2 and not flush_l2) else 1
+    descs, epis, keep = [desc], [epi if gemms == 2 else None], []
+    for _ in range(1, copies):
+        ac_i, img_i = ac.clone(), img.clone()
+        keep += [ac_i, img_i]
+        descs.append(sp24.make_desc(ac_i, img_i, b, m, n, k, meta_format=sp24.META_TC, c_f32=c32,
+                                    c_bf16=c16, alpha=alpha, dtype=lib_dt))
+        if gemms == 2:
+            au_i, iu_i = ac_up.clone(), img_up.clone()
+            keep += [au_i, iu_i]
+            e_i = sp24.Epilogue()
+            e_i.act = sp24.ACT_SILU
+            e_i.a_c_up, e_i.lda_c_up = au_i.data_ptr(), au_i.stride(0)
+            e_i.meta_up, e_i.alpha_up = iu_i.data_ptr(), 1.0
+            epis.append(e_i)
     if flush_l2:
         flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
         flush_out = torch.empty((), device=dev)
@@ -434,8 +475,44 @@ def main():
         flush_buf.zero_()
         torch.sum(flush_buf, dim=0, out=flush_out)
 
-    for _ in range(args.warmup):
-        step()
+    def step(i=0, st=None):
+        j = i % copies
+        sp = sptr if st is None else st
+        if gemms == 2:
+            rc = lib.sp24_gemm_fused(ctypes.byref(descs[j]), ctypes.byref(epis[j]), sp)
+        else:
+            rc = lib.sp24_gemm(ctypes.byref(descs[j]), sp)
+        if rc != 0:
+            raise sp24.Sp24Error(rc, "sp24_gemm")
+
+    for i in range(args.warmup):
+        step(i)
+
+    # Rotating steps of ~20 us would be paced by Python's launch rate, so they
+    # run as CUDA graphs: one graph of `copies` launches (one per weight copy)
+    # replayed K // copies times, plus one graph of the K % copies remaining
+    # launches -- exactly K sp24 launches, back to back on the device.
+    graphs, graph_error = None, None
+    if copies > 1 and not args.no_graph:
+        try:
+            torch.cuda.synchronize()
+            graphs = []
+            for cnt in (copies, args.steps % copies):
+                if cnt == 0:
+                    graphs.append(None)
+                    continue
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    cs = torch.cuda.current_stream().cuda_stream
+                    for i in range(cnt):
+                        step(i, cs)
+                graphs.append(gr)
+            for _ in range(2):
+                graphs[0].replay()
+            torch.cuda.synchronize()
+        except Exception as exc:   # reported in the line; eager launches are timed instead
+            graphs = None
+            graph_error = f"{type(exc).__name__}: {exc}"
     torch.cuda.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -453,10 +530,17 @@ def main():
                 step()
                 a1.record(stream)
                 evs.append((a0, a1))
+        elif graphs is not None:
+            e0.record(stream)
+            for _ in range(args.steps // copies):
+                graphs[0].replay()
+            if graphs[1] is not None:
+                graphs[1].replay()
+            e1.record(stream)
         else:
             e0.record(stream)
-            for _ in range(args.steps):
-                step()
+            for i in range(args.steps):
+                step(i)
             e1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -478,31 +562,60 @@ def main():
     if gemms == 2:
         g16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
         u16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-        dg = sp24.make_desc(ac, img, b, m, n, k, meta_format=sp24.META_TC, c_bf16=g16,
-                            dtype=lib_dt)
-        du = sp24.make_desc(ac_up, img_up, b, m, n, k, meta_format=sp24.META_TC, c_bf16=u16,
-                            dtype=lib_dt)
+        dgs, dus = [], []
+        for j in range(copies):
+            wg = (ac, img) if j == 0 else (keep[4 * (j - 1)], keep[4 * (j - 1) + 1])
+            wu = (ac_up, img_up) if j == 0 else (keep[4 * (j - 1) + 2], keep[4 * (j - 1) + 3])
+            dgs.append(sp24.make_desc(wg[0], wg[1], b, m, n, k, meta_format=sp24.META_TC,
+                                      c_bf16=g16, dtype=lib_dt))
+            dus.append(sp24.make_desc(wu[0], wu[1], b, m, n, k, meta_format=sp24.META_TC,
+                                      c_bf16=u16, dtype=lib_dt))
 
-        def unfused_step():
-            lib.sp24_gemm(ctypes.byref(dg), sptr)
-            lib.sp24_gemm(ctypes.byref(du), sptr)
+        def unfused_step(i=0, st=None):
+            sp = sptr if st is None else st
+            lib.sp24_gemm(ctypes.byref(dgs[i % copies]), sp)
+            lib.sp24_gemm(ctypes.byref(dus[i % copies]), sp)
             torch.mul(torch.nn.functional.silu(g16), u16, out=c16)
 
-        for _ in range(3):
-            unfused_step()
+        for i in range(3):
+            unfused_step(i)
         torch.cuda.synchronize()
-        uevs = []
-        for _ in range(min(args.steps, 50)):
-            if flush_l2:
+        ureps = min(args.steps, 50)
+        if flush_l2:
+            uevs = []
+            for _ in range(ureps):
                 clean_l2()
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                unfused_step()
+                a1.record(stream)
+                uevs.append((a0, a1))
+            torch.cuda.synchronize()
+            ums = sum(x.elapsed_time(y) for x, y in uevs) / len(uevs)
+        else:
+            ug = None
+            if graphs is not None:   # same launch path as the fused steps
+                ug = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(ug):
+                    cs = torch.cuda.current_stream().cuda_stream
+                    for i in range(copies):
+                        unfused_step(i, cs)
+                ug.replay()
+                torch.cuda.synchronize()
+                ureps = max(1, args.steps // copies) * copies
             a0 = torch.cuda.Event(enable_timing=True)
             a1 = torch.cuda.Event(enable_timing=True)
             a0.record(stream)
-            unfused_step()
+            if ug is not None:
+                for _ in range(ureps // copies):
+                    ug.replay()
+            else:
+                for i in range(ureps):
+                    unfused_step(i)
             a1.record(stream)
-            uevs.append((a0, a1))
-        torch.cuda.synchronize()
-        ums = sum(x.elapsed_time(y) for x, y in uevs) / len(uevs)
+            torch.cuda.synchronize()
+            ums = a0.elapsed_time(a1) / ureps
         unfused = {"ms_per_step": ums, "launches_per_step": 2 + 2,
                    "what": "two sp24_gemm calls (bf16 out) + torch silu(g) * u"}
 
@@ -755,6 +868,11 @@ def main():
                        "parallelism": f"N-shard x{world}, A + metadata replicated, no collective",
                        "l2": ("cleaned before every step (256 MB write, then read); "
                               "per-step CUDA events" if flush_l2 else
+                              f"{copies} weight copies ({copies * weight_bytes / 1e6:.0f} MB, "
+                              "over twice the 126 MB L2) rotated, steps back to back between "
+                              "one pair of CUDA events"
+                              + (" (CUDA graph replay)" if graphs is not None else
+                                 " (eager launches)") if copies > 1 else
                               "no flush: inputs + outputs exceed twice the 126 MB L2")},
             "pct_of_sparse_peak": 100.0 * kernel_tflops / sparse_peak,
             "roofline": roofline,
@@ -769,6 +887,8 @@ def main():
             line["fused_allgather"] = fused_ag
         if unfused:
             line["unfused_comparison"] = unfused
+        if graph_error:
+            line["graph_error"] = graph_error
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
