@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/sp24.h"
 #include "sp24_gemm2sm_kernel.cuh"
@@ -178,6 +179,44 @@ struct Prepared {
   int stall_producer;
 };
 
+// GEMM launches carry programmatic stream serialization: the kernel may be
+// scheduled while the previous kernel of the stream finishes, runs its
+// prologue (barriers, TMEM allocation, tensor-map prefetch), and its TMA
+// producers wait for the previous grid (griddepcontrol.wait) before the
+// first load.  SP24_PDL=0 launches without the attribute.
+bool pdl_enabled() {
+  const char* env = std::getenv("SP24_PDL");
+  return env == nullptr || std::atoi(env) != 0;
+}
+
+template <typename... KArgs, typename... Args>
+sp24_status launch_gemm_kernel(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                               cudaStream_t stream, unsigned cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned na = 0;
+  if (cluster > 0) {   // run-time cluster shape; 0 = none (or the kernel's __cluster_dims__)
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  SP24_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+  return SP24_OK;
+}
+
 template <int DT, int BN>
 sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
   using C = sp24::GemmCfg<DT, BN>;
@@ -229,9 +268,8 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
   const int grid = std::min(P.num_tiles, di.sm_count);
-  kern<<<grid, sp24::kThreads, C::SMEM_BYTES, stream>>>(ta, tb, P);
-  SP24_CUDA_TRY(cudaGetLastError());
-  return SP24_OK;
+  return launch_gemm_kernel(kern, static_cast<unsigned>(grid), sp24::kThreads, C::SMEM_BYTES, stream,
+                            0, ta, tb, P);
 }
 
 
@@ -314,9 +352,9 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
 
   const sp24::PairParams P = pair_params(p, C::BKD, 256, 256);
   const int pairs = std::max(1, std::min(P.num_tiles, di.sm_count / 2));
-  kern<<<2 * pairs, sp24::kPairThreads, C::SMEM_BYTES, stream>>>(ta, tb, te, P);
-  SP24_CUDA_TRY(cudaGetLastError());
-  return SP24_OK;
+  // Cluster shape (2) comes from the kernel's __cluster_dims__.
+  return launch_gemm_kernel(kern, static_cast<unsigned>(2 * pairs), sp24::kPairThreads,
+                            C::SMEM_BYTES, stream, 0, ta, tb, te, P);
 }
 
 // Largest cluster of split-K CTAs the device keeps resident `tiles` times
@@ -436,20 +474,9 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   const int tiles = P.m_blocks * P.n_tiles;
   P.splits = choose_splits(kern, C::SMEM_BYTES, tiles, P.stages, di.sm_count);
 
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * P.splits));
-  cfg.blockDim = dim3(sp24::kThreads);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(P.splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  SP24_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, ta2, P));
-  return SP24_OK;
+  // Launched with an explicit cluster shape of S CTAs, S = 1 included.
+  return launch_gemm_kernel(kern, static_cast<unsigned>(tiles * P.splits), sp24::kThreads,
+                            C::SMEM_BYTES, stream, static_cast<unsigned>(P.splits), ta, tb, ta2, P);
 }
 
 // Stage granularity of the CTA-pair kernel (PairCfg FINE); SP24_PAIR_FINE=0|1

@@ -297,8 +297,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   const uint64_t tmo = P.timeout_ns;
+  griddep_launch_dependents();
 
   if (warp == 0 || warp == kPairBWarp) {
+    griddep_wait();   // inputs may come from the previous kernel in the stream
     // ------------------------------------------------------------ producers
     // Two warps load each stage: warp 0 the A_c box (lane 0) and the metadata
     // atoms (lanes 1..E_PER), warp 10 the B boxes (one per lane).  Splitting

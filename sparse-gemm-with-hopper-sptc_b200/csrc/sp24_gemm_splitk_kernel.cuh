@@ -257,8 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   const uint64_t tmo = P.timeout_ns;
+  griddep_launch_dependents();
 
   if (warp == 0) {
+    griddep_wait();   // inputs may come from the previous kernel in the stream
     // ------------------------------------------------------------ producer
     // Lane l issues copy l of every stage: A boxes (gate units, then up
     // units), then B boxes, then metadata atoms (gate, then up).

@@ -144,6 +144,19 @@ SP24_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uin
   }
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A GEMM launched with programmatic stream serialization may start while the
+// previous kernel of the stream is still finishing.  It triggers its own
+// dependents once its prologue is done, and every thread that reads global
+// memory written by earlier work (the TMA producers) first waits for the
+// previous grid's completion and memory flush.  Everything else (epilogue
+// loads and stores) is ordered after that wait through the mbarrier chain.
+// Without the launch attribute both instructions are no-ops.
+SP24_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SP24_DEV void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 SP24_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
