@@ -386,6 +386,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true",
                     help="rotating (L2-sized) workloads: launch every step from Python instead "
                          "of replaying CUDA graphs of the same launches")
+    ap.add_argument("--no-static-hint", action="store_true",
+                    help="rotating workloads: do not pass SP24_HINT_STATIC_WEIGHTS")
     ap.add_argument("--steps-ref", type=int, default=1)
     ap.add_argument("--warmup-ref", type=int, default=1)
     args = ap.parse_args()
@@ -474,6 +476,13 @@ def main():
     def clean_l2():
         flush_buf.zero_()
         torch.sum(flush_buf, dim=0, out=flush_out)
+
+    # Rotating (decode-style) steps read weights that no in-flight work
+    # writes: say so, so the narrow-N kernel may start loading them while the
+    # previous launch finishes (B and C keep stream order).
+    static_hint = copies > 1 and not args.no_static_hint
+    if static_hint:
+        sp24.set_launch_hints(sp24.HINT_STATIC_WEIGHTS)
 
     def step(i=0, st=None):
         j = i % copies
@@ -872,7 +881,9 @@ def main():
                               "over twice the 126 MB L2) rotated, steps back to back between "
                               "one pair of CUDA events"
                               + (" (CUDA graph replay)" if graphs is not None else
-                                 " (eager launches)") if copies > 1 else
+                                 " (eager launches)")
+                              + (", SP24_HINT_STATIC_WEIGHTS" if static_hint else "")
+                              if copies > 1 else
                               "no flush: inputs + outputs exceed twice the 126 MB L2")},
             "pct_of_sparse_peak": 100.0 * kernel_tflops / sparse_peak,
             "roofline": roofline,

@@ -159,6 +159,22 @@ sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream);
    (No reference counterpart: the reference never bounds a wait.) */
 sp24_status sp24_last_kernel_status(sp24_stream_t stream);
 
+/* Launch hints for later GEMM calls made from the calling host thread (no
+   reference counterpart).  GEMM kernels are launched with programmatic
+   dependent launch: they may start while the previous kernel of the stream
+   finishes and wait for it before their first load.
+   SP24_HINT_STATIC_WEIGHTS: the caller guarantees that A_c and the metadata
+   image (SP24_META_TC) of later calls are not written by work still in flight
+   in the stream -- inference weights.  The narrow-N kernel then issues its
+   first ring of A_c and metadata loads before that wait, hiding their HBM
+   latency behind the previous kernel; B is still read, and C written, only
+   after the wait.  Ignored for SP24_META_REF / SP24_META_K16, whose image the
+   library itself writes just before the GEMM.  Default: SP24_HINT_NONE. */
+#define SP24_HINT_NONE 0u
+#define SP24_HINT_STATIC_WEIGHTS 1u
+void sp24_set_launch_hints(unsigned hints);
+unsigned sp24_get_launch_hints(void);
+
 /* Self-test of the bounded-wait path (no reference counterpart): launches the
    GEMM of `d` with a producer that issues no load, so the consumers' waits run
    out after `timeout_ns`; the kernel frees its TMEM and returns.  Requires

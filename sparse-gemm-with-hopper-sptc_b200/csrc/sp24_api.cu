@@ -151,6 +151,9 @@ CUtensorMapSwizzle swizzle_for_span(int span) {
   }
 }
 
+// Launch hints of the calling host thread (sp24_set_launch_hints).
+thread_local unsigned g_launch_hints = SP24_HINT_NONE;
+
 // Everything a launch needs after validation / workspace staging.
 struct Prepared {
   sp24_dtype dt;
@@ -174,6 +177,7 @@ struct Prepared {
   const float* bias_up;
   int gate_from_c;
   sp24::PeerOut peers;
+  int static_weights;   // SP24_HINT_STATIC_WEIGHTS in effect (narrow-N kernel)
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -468,6 +472,7 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.status = p.status;
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
+  P.static_weights = p.static_weights;
   P.meta_up = p.meta_up;
   P.alpha_up = p.alpha_up;
   P.bias_up = p.bias_up;
@@ -727,6 +732,8 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   p.status = d->status_dev ? d->status_dev : di->status_word;
   p.timeout_ns = timeout_ns;
   p.stall_producer = stall;
+  p.static_weights =
+      (g_launch_hints & SP24_HINT_STATIC_WEIGHTS) != 0 && d->meta_format == SP24_META_TC ? 1 : 0;
 
   if (d->meta_format == SP24_META_REF) {
     st = sp24_repack_meta(d->dtype, d->meta, d->m, d->k, ws + w.meta_off,
@@ -954,6 +961,10 @@ sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long ti
   SP24_CUDA_TRY(cudaStreamSynchronize(s));
   return h ? SP24_ERR_TIMEOUT : SP24_OK;
 }
+
+void sp24_set_launch_hints(unsigned hints) { g_launch_hints = hints; }
+
+unsigned sp24_get_launch_hints(void) { return g_launch_hints; }
 
 sp24_status sp24_last_kernel_status(sp24_stream_t stream) {
   DeviceInfo* di = nullptr;

@@ -68,6 +68,8 @@ struct SplitParams {
   const float* bias_up;
   int vec_f32;
   int vec_bf16;
+  int static_weights;  // A_c / metadata not written by in-flight work: the first
+                       // ring of their loads may precede griddepcontrol.wait
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -260,7 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_launch_dependents();
 
   if (warp == 0) {
-    griddep_wait();   // inputs may come from the previous kernel in the stream
+    // Inputs may come from the previous kernel in the stream: wait for it
+    // before the first load (with static weights, after the first ring of
+    // weight loads; see below).
+    if (!P.static_weights) griddep_wait();
     // ------------------------------------------------------------ producer
     // Lane l issues copy l of every stage: A boxes (gate units, then up
     // units), then B boxes, then metadata atoms (gate, then up).
@@ -284,33 +289,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int dx = is_a ? KB * C::A_COLS : 0;
       const int dy = is_b ? C::BKD : 0;
       int atom = g0 * C::E_S + (up ? el - C::E_S : el);
-      int s = 0;
-      uint32_t ph = 0, soff = 0;
-      uint32_t issued_mask = 0, issued_ph = 0;
+      auto issue = [&](int slot, uint32_t slot_off) {
+        uint8_t* dst = smem + slot_off + off;
+        if (is_a) {
+          tma_load_2d(dst, amap, &full_bar[slot], x, y);
+        } else if (is_b) {
+          tma_load_2d(dst, &tmB, &full_bar[slot], x, y);
+        } else if (atom < P.katoms) {
+          bulk_load(dst, meta + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
+                    kAtomBytes, &full_bar[slot]);
+        }
+        x += dx;
+        y += dy;
+        atom += C::E_S;
+      };
+      // Static weights: the first ring of A_c and metadata copies (free
+      // slots) goes out before the wait for the previous grid; B, which that
+      // grid may have produced, follows it.
+      const int pre = P.static_weights ? min(C::STAGES, nst) : 0;
+      if (P.static_weights) {
+        if (!is_b)
+          for (int i = 0; i < pre; ++i) issue(i, static_cast<uint32_t>(i * C::STAGE_BYTES));
+        griddep_wait();
+        if (is_b)
+          for (int i = 0; i < pre; ++i) issue(i, static_cast<uint32_t>(i * C::STAGE_BYTES));
+      }
+      int s = pre % C::STAGES;
+      uint32_t ph = pre == C::STAGES ? 1u : 0u;
+      uint32_t soff = static_cast<uint32_t>(s * C::STAGE_BYTES);
+      uint32_t issued_mask = pre > 0 ? (1u << pre) - 1u : 0u, issued_ph = 0;
       bool ok = true;
-      for (int i = 0; i < nst; ++i) {
+      for (int i = pre; i < nst; ++i) {
         int good = 1;
         if (lane == 0) good = mbar_wait_fast(&empty_bar[s], ph ^ 1u, &abort_sh, tmo) ? 1 : 0;
         if (__shfl_sync(C::LOAD_LANES, good, 0) == 0) {
           ok = false;
           break;
         }
-        uint8_t* dst = smem + soff + off;
-        if (is_a) {
-          tma_load_2d(dst, amap, &full_bar[s], x, y);
-        } else if (is_b) {
-          tma_load_2d(dst, &tmB, &full_bar[s], x, y);
-        } else if (atom < P.katoms) {
-          bulk_load(dst, meta + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
-                    kAtomBytes, &full_bar[s]);
-        }
+        issue(s, soff);
         if (lane == 0) {
           issued_mask |= 1u << s;
           issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
         }
-        x += dx;
-        y += dy;
-        atom += C::E_S;
         soff += C::STAGE_BYTES;
         if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
       }

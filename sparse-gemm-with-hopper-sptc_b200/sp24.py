@@ -39,8 +39,10 @@ EXPORTS = [
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
     "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused", "sp24_repack_meta_k16",
     "sp24_gemm_allgather", "sp24_ipc_get_handle", "sp24_ipc_open_handle", "sp24_ipc_close",
+    "sp24_set_launch_hints", "sp24_get_launch_hints",
 ]
 MAX_PEERS = 7
+HINT_NONE, HINT_STATIC_WEIGHTS = 0, 1
 
 ACT_NONE, ACT_SILU = 0, 1
 
@@ -104,6 +106,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_ipc_close.argtypes = [c_void_p]
     lib.sp24_selftest_timeout.argtypes = [POINTER(GemmDesc), c_ulonglong, c_void_p]
     lib.sp24_last_kernel_status.argtypes = [c_void_p]
+    lib.sp24_set_launch_hints.argtypes = [ctypes.c_uint]
+    lib.sp24_set_launch_hints.restype = None
+    lib.sp24_get_launch_hints.restype = ctypes.c_uint
     lib.sp24_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
                                   c_void_p, c_void_p, POINTER(c_longlong), c_void_p]
     lib.sp24_prune_2of4.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
@@ -325,6 +330,16 @@ def gemm_allgather(desc: GemmDesc, peer_f32=(), peer_bf16=(), stream=None) -> No
         po.c_bf16[i] = a
     _check(load().sp24_gemm_allgather(ctypes.byref(desc), ctypes.byref(po), _stream(stream)),
            "sp24_gemm_allgather")
+
+
+def set_launch_hints(hints: int) -> None:
+    """sp24_set_launch_hints for later GEMM calls of this thread
+    (HINT_STATIC_WEIGHTS: A_c / metadata images are not written by in-flight work)."""
+    load().sp24_set_launch_hints(hints)
+
+
+def get_launch_hints() -> int:
+    return load().sp24_get_launch_hints()
 
 
 def last_kernel_status(stream=None) -> int:

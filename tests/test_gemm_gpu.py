@@ -10,6 +10,7 @@ Tolerances, as the reference and the north star state them:
   * compressed values, metadata, metadata images, pruning and e4m3
     quantisation: bit-exact.
 """
+import ctypes
 import os
 
 import numpy as np
@@ -318,6 +319,75 @@ def test_splitk_mlp_shapes_default_dispatch():
         err = oracle.row_norm_rel_error(c[rows].cpu().numpy(), ref, oracle.to_float(1, a_bits),
                                         oracle.to_float(1, b_bits))
         assert err <= 1e-2, err
+
+
+def _layer_chain(hints, meta_format, graph, steps=6, t=16, d=2048):
+    """A decode-style chain: x_{i+1} = bf16(W_i x_i) through `steps` square
+    2:4 layers, each GEMM reading the previous one's output as B, all on one
+    stream (eagerly or as one captured CUDA graph)."""
+    g = torch.Generator(device=DEV).manual_seed(77)
+    ws = []
+    for _ in range(steps):
+        w = (torch.randn((d, d), device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+        ac, meta = sp24.compress(sp24.prune_2of4(w))
+        img = sp24.repack_meta(meta, d, d, torch.bfloat16)
+        ws.append((ac, img if meta_format == sp24.META_TC else meta))
+    xs = [torch.randn((d, t), device=DEV, generator=g).to(torch.bfloat16)]
+    xs += [torch.empty((d, t), device=DEV, dtype=torch.bfloat16) for _ in range(steps)]
+    wsp = torch.empty(1 << 22, dtype=torch.uint8, device=DEV)
+    descs = [sp24.make_desc(ac, mt, xs[i], d, t, d, meta_format=meta_format, c_bf16=xs[i + 1],
+                            workspace=wsp) for i, (ac, mt) in enumerate(ws)]
+    lib = sp24.load()
+    old = sp24.get_launch_hints()
+    sp24.set_launch_hints(hints)
+    try:
+        def run(stream):
+            for dsc in descs:
+                assert lib.sp24_gemm(ctypes.byref(dsc), stream) == 0
+        if graph:
+            gr = torch.cuda.CUDAGraph()
+            run(torch.cuda.current_stream().cuda_stream)   # warm-up outside capture
+            torch.cuda.synchronize()
+            for x in xs[1:]:
+                x.fill_(float("nan"))
+            with torch.cuda.graph(gr):
+                run(torch.cuda.current_stream().cuda_stream)
+            for _ in range(3):
+                gr.replay()
+        else:
+            for _ in range(3):
+                run(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+    finally:
+        sp24.set_launch_hints(old)
+    return [x.clone() for x in xs[1:]]
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_static_weight_hint_keeps_stream_order(graph):
+    """SP24_HINT_STATIC_WEIGHTS lets the narrow-N kernel load weights before
+    the previous kernel ends; B (the previous layer's output) must still be
+    read after it: a chain of layers gives bit-identical activations with and
+    without the hint, eagerly and from a CUDA graph, and with reference-layout
+    metadata (repacked in-stream, so the hint is ignored)."""
+    base = _layer_chain(sp24.HINT_NONE, sp24.META_TC, graph)
+    hinted = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_TC, graph)
+    for a, b in zip(base, hinted):
+        assert torch.isfinite(a.float()).all()
+        assert torch.equal(a, b)
+    ref_fmt = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_REF, graph)
+    for a, b in zip(base, ref_fmt):
+        assert torch.equal(a, b)
+
+
+def test_pdl_off_matches_pdl_on():
+    """Launches without programmatic dependent launch (SP24_PDL=0) give the
+    same chain bit for bit."""
+    on = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_TC, False)
+    off = _with_env({"SP24_PDL": "0"},
+                    lambda: _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_TC, False))
+    for a, b in zip(on, off):
+        assert torch.equal(a, b)
 
 
 # ------------------------------------------------------------------ e4m3 configuration
