@@ -110,6 +110,15 @@ def profile_traffic(tag):
     return None
 
 
+def job_gpus(world):
+    """nvidia-smi ids of the GPUs this job's ranks use (local rank r -> CUDA
+    device r), through CUDA_VISIBLE_DEVICES when it is set, so idle GPUs of
+    the node stay out of the clock record."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    ids = [x.strip() for x in vis.split(",") if x.strip()] if vis else [str(i) for i in range(world)]
+    return ids[:world]
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -526,7 +535,7 @@ def main():
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(range(torch.cuda.device_count()) if rank == 0 else [local]) as clk:
+    with ClockSampler(job_gpus(world) if rank == 0 else job_gpus(world)[local:local + 1]) as clk:
         torch.cuda.synchronize()
         barrier()
         if flush_l2:
