@@ -473,6 +473,8 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
   P.static_weights = p.static_weights;
+  const char* krot = std::getenv("SP24_KROT");   // 0: every tile in K order (tuning runs)
+  P.rotate = (krot == nullptr || std::atoi(krot) != 0) ? 1 : 0;
   P.meta_up = p.meta_up;
   P.alpha_up = p.alpha_up;
   P.bias_up = p.bias_up;

@@ -68,6 +68,7 @@ struct SplitParams {
   const float* bias_up;
   int vec_f32;
   int vec_bf16;
+  int rotate;          // per-tile rotation of the K order (see the kernel)
   int static_weights;  // A_c / metadata not written by in-flight work: the first
                        // ring of their loads may precede griddepcontrol.wait
   int* status;
@@ -230,6 +231,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int g0 = static_cast<int>(static_cast<long long>(P.stages) * rank / S);
   const int g1 = static_cast<int>(static_cast<long long>(P.stages) * (rank + 1) / S);
   const int nst = g1 - g0;
+  // K order rotated per row block (P.rotate): the tiles of row block mb start
+  // at stage mb * nst / m_blocks of their range and wrap around.  B is shared
+  // by every row block, and with one order for all, the CTAs that stream at
+  // the same time all read the same few rows of B -- the same L2 lines -- at
+  // the same moment.  The rotation depends on mb alone, so a column shard of
+  // C (N-sharding) sums every element in the same order as the full GEMM.
+  const int rot = (P.rotate && nst > 0)
+                      ? static_cast<int>(static_cast<long long>(mb) * nst / P.m_blocks)
+                      : 0;
+  auto stage_of = [&](int i) {   // i-th stage this CTA processes (i < 2 nst)
+    const int j = i + rot;
+    return g0 + (j >= nst ? j - nst : j);
+  };
 
   if (threadIdx.x == 0) {
     abort_sh = 0;
@@ -243,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // First use of every slot armed here; the MMA warp re-arms each slot for
     // its next stage when it sees the slot fill.
     for (int s = 0; s < C::STAGES && s < nst; ++s)
-      mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, g0 + s));
+      mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, stage_of(s)));
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -283,25 +297,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                            : is_b ? static_cast<uint32_t>(C::A_BYTES + u * C::B_UNIT +
                                                           (bl % C::B_BOXES) * C::B_BOX_BYTES)
                                   : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + el * kAtomBytes);
-      int x = is_a ? (g0 * KB + u) * C::A_COLS
-                   : (is_b ? nb * BN + (bl % C::B_BOXES) * C::B_BOXN : 0);
-      int y = is_a ? mb * kBlockM : (is_b ? (g0 * KB + u) * C::UK : 0);
-      const int dx = is_a ? KB * C::A_COLS : 0;
-      const int dy = is_b ? C::BKD : 0;
-      int atom = g0 * C::E_S + (up ? el - C::E_S : el);
-      auto issue = [&](int slot, uint32_t slot_off) {
+      const int b_x = nb * BN + (bl % C::B_BOXES) * C::B_BOXN;
+      const int e_off = up ? el - C::E_S : el;
+      // Copy of this lane for global stage gs into ring slot `slot`.
+      auto issue = [&](int slot, uint32_t slot_off, int gs) {
         uint8_t* dst = smem + slot_off + off;
         if (is_a) {
-          tma_load_2d(dst, amap, &full_bar[slot], x, y);
+          tma_load_2d(dst, amap, &full_bar[slot], (gs * KB + u) * C::A_COLS, mb * kBlockM);
         } else if (is_b) {
-          tma_load_2d(dst, &tmB, &full_bar[slot], x, y);
-        } else if (atom < P.katoms) {
-          bulk_load(dst, meta + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
-                    kAtomBytes, &full_bar[slot]);
+          tma_load_2d(dst, &tmB, &full_bar[slot], b_x, (gs * KB + u) * C::UK);
+        } else {
+          const int atom = gs * C::E_S + e_off;
+          if (atom < P.katoms)
+            bulk_load(dst, meta + (static_cast<size_t>(atom) * P.meta_mblocks + mb) * kAtomBytes,
+                      kAtomBytes, &full_bar[slot]);
         }
-        x += dx;
-        y += dy;
-        atom += C::E_S;
       };
       // Static weights: the first ring of A_c and metadata copies (free
       // slots) goes out before the wait for the previous grid; B, which that
@@ -309,10 +319,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pre = P.static_weights ? min(C::STAGES, nst) : 0;
       if (P.static_weights) {
         if (!is_b)
-          for (int i = 0; i < pre; ++i) issue(i, static_cast<uint32_t>(i * C::STAGE_BYTES));
+          for (int i = 0; i < pre; ++i)
+            issue(i, static_cast<uint32_t>(i * C::STAGE_BYTES), stage_of(i));
         griddep_wait();
         if (is_b)
-          for (int i = 0; i < pre; ++i) issue(i, static_cast<uint32_t>(i * C::STAGE_BYTES));
+          for (int i = 0; i < pre; ++i)
+            issue(i, static_cast<uint32_t>(i * C::STAGE_BYTES), stage_of(i));
       }
       int s = pre % C::STAGES;
       uint32_t ph = pre == C::STAGES ? 1u : 0u;
@@ -326,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        issue(s, soff);
+        issue(s, soff, stage_of(i));
         if (lane == 0) {
           issued_mask |= 1u << s;
           issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
@@ -353,13 +365,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ph = 0, soff = 0, ebuf = 0;
     bool ok = true, any = false;
     for (int i = 0; i < nst; ++i) {
-      const int g = g0 + i;
+      const int g = stage_of(i);
       if (!mbar_wait_warp(&full_bar[s], ph, &abort_sh, tmo)) {
         ok = false;
         break;
       }
       if (lane == 0 && i + C::STAGES < nst)
-        mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, g + C::STAGES));
+        mbar_arrive_expect_tx(&full_bar[s], split_stage_tx<C>(P, stage_of(i + C::STAGES)));
       tc_fence_after();
       ebuf ^= static_cast<uint32_t>(G * C::E_S * 4);
       const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
