@@ -327,10 +327,10 @@ sp24_status encode_meta_rows(CUtensorMap* te, const Prepared& p) {
                    8, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-template <int DT, int FINE>
+template <int DT, int FINE, int BNP = 256>
 sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
-  using C = sp24::PairCfg<DT, FINE>;
-  auto kern = sp24::sp24_gemm2sm_kernel<DT, FINE>;
+  using C = sp24::PairCfg<DT, FINE, BNP>;
+  auto kern = sp24::sp24_gemm2sm_kernel<DT, FINE, BNP>;
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   SP24_CUDA_TRY(cudaGetDevice(&dev));
@@ -349,12 +349,12 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   if (st != SP24_OK) return st;
   st = encode_2d(&tb, tdt, p.b, static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.k),
                  static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::BKD,
-                 CU_TENSOR_MAP_SWIZZLE_128B);
+                 swizzle_for_span(C::B_SPAN));
   if (st != SP24_OK) return st;
   st = encode_meta_rows(&te, p);
   if (st != SP24_OK) return st;
 
-  const sp24::PairParams P = pair_params(p, C::BKD, 256, 256);
+  const sp24::PairParams P = pair_params(p, C::BKD, 256, BNP);
   const int pairs = std::max(1, std::min(P.num_tiles, di.sm_count / 2));
   // Cluster shape (2) comes from the kernel's __cluster_dims__.
   return launch_gemm_kernel(kern, static_cast<unsigned>(2 * pairs), sp24::kPairThreads,
@@ -505,6 +505,27 @@ bool use_pair_kernel(int m, int n, int hint) {
   return m >= 256 && n >= 256;
 }
 
+// Narrow N (33..128 columns) with enough 256-row tiles to occupy most SMs
+// as CTA pairs: the pair kernel with a 64- or 128-wide tile.  Its
+// cta_group::2 MMAs split B over the two SMs, so each stages half of it, and
+// the ring holds 6-8 stages; the split-K kernel, one SM per 128-row tile,
+// streams a full B per tile and is latency-bound there (W_up, T = 128).
+// Returns the tile width or 0.  SP24_NARROW_PAIR=0 turns it off, =1 forces it
+// for every eligible shape (tests and tuning runs).
+int narrow_pair_width(const sp24_gemm_desc* d, int sm_count) {
+  const char* env = std::getenv("SP24_NARROW_PAIR");
+  const int mode = env != nullptr ? std::atoi(env) : -1;
+  if (mode == 0) return 0;
+  const char* kern = std::getenv("SP24_KERNEL");
+  if (kern != nullptr && mode != 1) return 0;   // a forced kernel choice wins
+  if (d->tile_n != 0 || d->n <= 32 || d->n > 128) return 0;
+  const int np = d->n <= 64 ? 64 : 128;
+  if (mode == 1) return np;
+  const long long pair_tiles =
+      static_cast<long long>((d->m + 255) / 256) * ((d->n + np - 1) / np);
+  return pair_tiles * 4 >= static_cast<long long>(sm_count / 2) * 3 ? np : 0;
+}
+
 // Tiles at most 128 wide take the split-K kernel when N itself is narrow or
 // the tile count is modest (up to four waves): there its large stages and
 // K splitting win.  With thousands of narrow tiles the persistent
@@ -529,6 +550,11 @@ int splitk_units(int bn) {
 }
 
 using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t);
+
+template <int DT>
+LaunchFn pick_narrow_pair(int np) {
+  return np == 64 ? launch_gemm2sm<DT, 0, 64> : launch_gemm2sm<DT, 0, 128>;
+}
 
 // Pair-kernel variant: the 256 x 256 tile with coarse stages, or its
 // fine-staged form (SP24_PAIR_FINE=1).
@@ -802,6 +828,13 @@ sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const Devic
     return pick_pair(d->dtype)(p, *di, stream);
   }
   const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);
+  const int np = narrow_pair_width(d, di->sm_count);
+  if (np > 0) {
+    LaunchFn nf = d->dtype == SP24_F16    ? pick_narrow_pair<0>(np)
+                  : d->dtype == SP24_BF16 ? pick_narrow_pair<1>(np)
+                                          : pick_narrow_pair<2>(np);
+    return nf(p, *di, stream);
+  }
   if (use_splitk_kernel(d->m, d->n, bn, di->sm_count)) {
     const int kb = splitk_units(bn);
     LaunchFn sf = d->dtype == SP24_F16    ? pick_splitk<0>(bn, kb)

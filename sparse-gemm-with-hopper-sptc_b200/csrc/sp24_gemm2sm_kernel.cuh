@@ -71,7 +71,10 @@ struct PairParams {
 // stage and twice as many stages.  A ring slot is freed only when its MMAs
 // complete, so the MMAs queued in the tensor pipe hold part of the ring; finer
 // stages leave more of the same shared memory loading.
-template <int DT, int FINE>
+// BNP is the pair tile width: 256 for large N; 128 or 64 for narrow N (an MLP
+// layer applied to 33..128 tokens), where each CTA stages only BNP / 2
+// columns of B, so a stage shrinks to 26-36 KB and the ring holds 6-8 of them.
+template <int DT, int FINE, int BNP = 256>
 struct PairCfg {
   static constexpr int ESZ = (DT == 2) ? 1 : 2;
   static constexpr int KIND = (DT == 2) ? 1 : 0;
@@ -85,15 +88,20 @@ struct PairCfg {
   static constexpr int A_BYTES = kBlockM * A_ROW;
   static constexpr uint32_t A_LAYOUT = A_ROW == 128 ? kLayoutSW128 : kLayoutSW64;
   static constexpr uint32_t A_SBO = 8 * A_ROW;                  // 8-row group stride
-  static constexpr int BN = 256;                                // pair tile width
-  static constexpr int BN_CTA = 128;                            // B columns staged per CTA
-  static constexpr int B_BOXN = 128 / ESZ;
+  static constexpr int BN = BNP;                                // pair tile width
+  static constexpr int BN_CTA = BNP / 2;                        // B columns staged per CTA
+  static constexpr int B_ROWB = BN_CTA * ESZ;                   // bytes of one K row of it
+  static constexpr int B_SPAN = B_ROWB >= 128 ? 128 : B_ROWB;   // swizzle span of a TMA box
+  static constexpr int B_BOXN = B_SPAN / ESZ;
   static constexpr int B_BOXES = BN_CTA / B_BOXN;
-  static constexpr int B_BOX_BYTES = 128 * BKD;
+  static constexpr int B_BOX_BYTES = B_SPAN * BKD;
   static constexpr int B_BYTES = B_BOX_BYTES * B_BOXES;
-  static constexpr uint32_t B_LBO = B_BOX_BYTES;                // MN-major SW128: chunk stride
-  static constexpr uint32_t B_SBO = 1024;                       // 8-row K group stride
-  static constexpr int B_MMA_ADVANCE = MMA_K * 128;
+  static constexpr uint32_t B_LAYOUT =
+      B_SPAN == 128 ? kLayoutSW128 : B_SPAN == 64 ? kLayoutSW64 : kLayoutSW32;
+  static constexpr uint32_t B_LBO = B_BOX_BYTES;                // MN-major swizzled: chunk stride
+  static constexpr uint32_t B_SBO = 8 * B_SPAN;                 // 8-row K group stride
+  static constexpr int B_MMA_ADVANCE = MMA_K * B_SPAN;
+  static constexpr int CW = BNP / 2;                            // columns per epilogue warp
   static constexpr int E_BYTES = E_PER * kAtomBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
   static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
@@ -103,7 +111,9 @@ struct PairCfg {
   static constexpr int E_COL = 256;                             // two buffers of E_PER*4 columns
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
-  static constexpr uint32_t IDESC = make_idesc_sparse(FMT, 256, 256, true);
+  static constexpr uint32_t IDESC = make_idesc_sparse(FMT, BNP, 256, true);
+  static_assert(BNP == 64 || BNP == 128 || BNP == 256, "pair tile width 64, 128 or 256");
+  static_assert(B_SPAN >= 32, "B rows of at least 32 bytes per CTA");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
   static_assert(LOADS <= 32, "one lane per TMA box");
@@ -125,47 +135,53 @@ SP24_DEV void st_global_v8_u32(void* p, const uint32_t* v) {
                : "memory");
 }
 
+template <int CW>
 SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
-                                const uint32_t (&r)[128], int row, int col0);
+                                const uint32_t (&r)[CW], int row, int col0);
 
-// Store 128 consecutive accumulator columns of one row (already in registers).
-SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[128], int row, int col0) {
+// Store CW consecutive accumulator columns of one row (already in registers).
+template <int CW>
+SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[CW], int row, int col0) {
   if (row >= P.m) return;
   // The epilogue is applied in place, so the stores below see final values.
   if (P.bias != nullptr || P.act != kActNone) {
     const bool hb = P.bias != nullptr;
     const float b = hb ? P.bias[row] : 0.0f;
 #pragma unroll
-    for (int i = 0; i < 128; ++i)
+    for (int i = 0; i < CW; ++i)
       r[i] = __float_as_uint(epi_value(__uint_as_float(r[i]), P.alpha, b, hb, P.act));
   } else if (P.alpha != 1.0f) {
 #pragma unroll
-    for (int i = 0; i < 128; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * P.alpha);
+    for (int i = 0; i < CW; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * P.alpha);
   }
-  if (P.gate_from_c) gate_mul_row<128>(P, reinterpret_cast<float*>(r), row, col0);
-  pair_store_row_to(P, P.c_f32, P.c_bf16, r, row, col0);
+  if (P.gate_from_c) gate_mul_row<CW>(P, reinterpret_cast<float*>(r), row, col0);
+  pair_store_row_to<CW>(P, P.c_f32, P.c_bf16, r, row, col0);
 }
 
 // Fused all-gather, warp-cooperative: after a warp has stored its 32 rows x
-// 128 columns locally (pair_store_row), it re-reads them from L2 with the
+// CW columns locally (pair_store_row), it re-reads them from L2 with the
 // lanes spread along each row and writes every row segment to the peers as
-// contiguous 512 B (fp32) / 256 B (bf16) runs, i.e. whole 128 B lines over
-// NVLink, instead of one scattered 32 B write per lane and row.
+// contiguous runs (512 B fp32 / 256 B bf16 at CW = 128), i.e. whole 128 B
+// lines over NVLink, instead of one scattered 32 B write per lane and row.
+template <int CW>
 SP24_DEV void pair_push_rows_to_peers(const PairParams& P, int row0, int col0) {
   __syncwarp();  // the warp's local stores are visible to its own loads
   const int lane = threadIdx.x & 31;
-  const bool full = col0 + 128 <= P.n;
+  const bool full = col0 + CW <= P.n;
+  const bool mine = 4 * lane < CW;   // lanes that cover the segment, 4 columns each
   for (int rr = 0; rr < 32; ++rr) {
     const int row = row0 + rr;
     if (row >= P.m) break;
     const long long o = static_cast<long long>(row) * P.ldc + col0;
     if (P.c_f32 != nullptr) {
       if (full && P.vec_f32) {
-        const float4 v = *reinterpret_cast<const float4*>(P.c_f32 + o + 4 * lane);
-        for (int p = 0; p < P.peers.n; ++p)
-          *reinterpret_cast<float4*>(P.peers.f32[p] + o + 4 * lane) = v;
+        if (mine) {
+          const float4 v = *reinterpret_cast<const float4*>(P.c_f32 + o + 4 * lane);
+          for (int p = 0; p < P.peers.n; ++p)
+            *reinterpret_cast<float4*>(P.peers.f32[p] + o + 4 * lane) = v;
+        }
       } else {
-        for (int c = lane; c < 128 && col0 + c < P.n; c += 32) {
+        for (int c = lane; c < CW && col0 + c < P.n; c += 32) {
           const float v = P.c_f32[o + c];
           for (int p = 0; p < P.peers.n; ++p) P.peers.f32[p][o + c] = v;
         }
@@ -173,11 +189,13 @@ SP24_DEV void pair_push_rows_to_peers(const PairParams& P, int row0, int col0) {
     }
     if (P.c_bf16 != nullptr) {
       if (full && P.vec_bf16) {
-        const uint2 v = *reinterpret_cast<const uint2*>(P.c_bf16 + o + 4 * lane);
-        for (int p = 0; p < P.peers.n; ++p)
-          *reinterpret_cast<uint2*>(P.peers.bf16[p] + o + 4 * lane) = v;
+        if (mine) {
+          const uint2 v = *reinterpret_cast<const uint2*>(P.c_bf16 + o + 4 * lane);
+          for (int p = 0; p < P.peers.n; ++p)
+            *reinterpret_cast<uint2*>(P.peers.bf16[p] + o + 4 * lane) = v;
+        }
       } else {
-        for (int c = lane; c < 128 && col0 + c < P.n; c += 32) {
+        for (int c = lane; c < CW && col0 + c < P.n; c += 32) {
           const __nv_bfloat16 v = P.c_bf16[o + c];
           for (int p = 0; p < P.peers.n; ++p) P.peers.bf16[p][o + c] = v;
         }
@@ -186,15 +204,16 @@ SP24_DEV void pair_push_rows_to_peers(const PairParams& P, int row0, int col0) {
   }
 }
 
-// Stores 128 finished values of one row (as float bits) into one copy of C.
+// Stores CW finished values of one row (as float bits) into one copy of C.
+template <int CW>
 SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
-                                const uint32_t (&r)[128], int row, int col0) {
-  const bool full = col0 + 128 <= P.n;
+                                const uint32_t (&r)[CW], int row, int col0) {
+  const bool full = col0 + CW <= P.n;
   if (c32 != nullptr) {
     float* dst = c32 + static_cast<long long>(row) * P.ldc + col0;
     if (full && P.vec_f32 == 2) {
 #pragma unroll
-      for (int i = 0; i < 128; i += 8) {
+      for (int i = 0; i < CW; i += 8) {
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]);
@@ -202,13 +221,13 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
       }
     } else if (full && P.vec_f32 == 1) {
 #pragma unroll
-      for (int i = 0; i < 128; i += 4)
+      for (int i = 0; i < CW; i += 4)
         *reinterpret_cast<float4*>(dst + i) =
             make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
                         __uint_as_float(r[i + 3]));
     } else {
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
+      for (int i = 0; i < CW; ++i)
         if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]);
     }
   }
@@ -216,7 +235,7 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
     __nv_bfloat16* dst = c16 + static_cast<long long>(row) * P.ldc + col0;
     if (full && P.vec_bf16 >= 1) {
 #pragma unroll
-      for (int i = 0; i < 128; i += 16) {
+      for (int i = 0; i < CW; i += 16) {
         uint32_t pk[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -233,19 +252,19 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
+      for (int i = 0; i < CW; ++i)
         if (col0 + i < P.n) dst[i] = __float2bfloat16_rn(__uint_as_float(r[i]));
     }
   }
 }
 
-template <int DT, int FINE>
+template <int DT, int FINE, int BNP>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     sp24_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmE, const PairParams P) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using C = PairCfg<DT, FINE>;
+  using C = PairCfg<DT, FINE, BNP>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -335,7 +354,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         pair_tile_coords(P, t, mp, nb);
         const int row0 = mp * 256 + static_cast<int>(rank) * 128;
         const int mb = mp * 2 + static_cast<int>(rank);
-        int x = is_b ? nb * 256 + static_cast<int>(rank) * 128 + lane * C::B_BOXN : 0;
+        int x = is_b ? nb * C::BN + static_cast<int>(rank) * C::BN_CTA + lane * C::B_BOXN : 0;
         int y = is_b ? 0 : (lane == 0 ? row0 : ((lane - 1) * P.m_blocks + mb) * 8);
         for (int ks = 0; ks < P.k_stages; ++ks) {
           int good = 1;
@@ -381,7 +400,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     if (leader) {
       const uint32_t smem_base = smem_u32(smem);
       const uint64_t adesc0 = make_sdesc(smem_base, 16, C::A_SBO, C::A_LAYOUT);
-      const uint64_t bdesc0 = make_sdesc(smem_base + C::A_BYTES, C::B_LBO, C::B_SBO, kLayoutSW128);
+      const uint64_t bdesc0 = make_sdesc(smem_base + C::A_BYTES, C::B_LBO, C::B_SBO, C::B_LAYOUT);
       const uint64_t edesc0 =
           make_sdesc(smem_base + C::A_BYTES + C::B_BYTES, kAtomBytes, 128, kLayoutNone);
       constexpr uint32_t SD = C::STAGE_BYTES >> 4;
@@ -471,19 +490,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                          static_cast<uint32_t>(half * 128);
-      uint32_t r[128];
-      tmem_ld_x32(tb + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld_x32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld_x32(tb + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      tmem_ld_x32(tb + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+                          static_cast<uint32_t>(half * C::CW);
+      uint32_t r[C::CW];
+#pragma unroll
+      for (int c = 0; c < C::CW; c += 32)
+        tmem_ld_x32(tb + static_cast<uint32_t>(c), *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
       tmem_ld_wait(r);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acce_leader);
       const int row = mp * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
-      pair_store_row(P, r, row, nb * 256 + half * 128);
-      if (P.peers.n > 0) pair_push_rows_to_peers(P, row - lane, nb * 256 + half * 128);
+      pair_store_row<C::CW>(P, r, row, nb * C::BN + half * C::CW);
+      if (P.peers.n > 0) pair_push_rows_to_peers<C::CW>(P, row - lane, nb * C::BN + half * C::CW);
       aph ^= 1u;
     }
   }

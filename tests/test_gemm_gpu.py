@@ -271,6 +271,62 @@ def _with_env(env, fn):
                 os.environ[k] = v
 
 
+NARROW_PAIR_CASES = [
+    # m, n, k: 64- and 128-wide pair tiles; ragged M (the second CTA's rows
+    # wholly past M), ragged N inside the tile, K tails, several tiles
+    (512, 64, 1024), (768, 100, 512), (1000, 128, 2048), (256, 40, 4096), (2048, 96, 256),
+    (384, 128, 1536),
+]
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k", NARROW_PAIR_CASES)
+def test_narrow_pair_matches_oracle(dt, m, n, k):
+    """The CTA-pair kernel with a 64- or 128-wide tile (33..128 columns):
+    within the row-norm bound of the oracle, bf16 output the rounding of the
+    fp32 output, and within fp32 rounding of the split-K kernel."""
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    gen = oracle.Gen(m + 13 * n + k)
+    a, b, _, _, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    b_t = to_dev(b, dt)
+
+    def run():
+        return sp24.gemm(ac_t, e_t, b_t, m, n, k, out_bf16=True, dtype=lib_dtype(dt))
+
+    c, cb = _with_env({"SP24_NARROW_PAIR": "1"}, run)
+    c_split, _ = _with_env({"SP24_NARROW_PAIR": "0", "SP24_KERNEL": "splitk"}, run)
+    torch.cuda.synchronize()
+    check_c(c, c_ref, a, b, dt, abs_rule=(k <= 1024))
+    assert torch.equal(cb, c.to(torch.bfloat16))
+    scale = c_split.abs().max().item() + 1.0
+    assert (c - c_split).abs().max().item() <= 1e-5 * scale
+
+
+@pytest.mark.parametrize("n", [64, 128])
+def test_narrow_pair_decode_and_epilogue(n):
+    """B = identity through the narrow pair tile gives A exactly; bias and
+    SiLU land on the right rows and columns."""
+    m, k = 512, 512
+    a = _decode_case(1, m, k, seed=n)
+    b = oracle.from_float(1, np.eye(k, n, dtype=np.float32))
+    ac_t, e_t = sp24.compress(to_dev(a, 1))
+    img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
+    b_t = to_dev(b, 1)
+    c, _ = _with_env({"SP24_NARROW_PAIR": "1"},
+                     lambda: sp24.gemm(ac_t, e_t, b_t, m, n, k, dtype=torch.bfloat16))
+    np.testing.assert_array_equal(c.cpu().numpy(), oracle.to_float(1, a)[:, :n])
+    bias = torch.linspace(-1, 1, m, device=DEV)
+    fused, _ = _with_env({"SP24_NARROW_PAIR": "1"},
+                         lambda: sp24.gemm_fused(ac_t, img, b_t, m, n, k, bias=bias,
+                                                 act=sp24.ACT_SILU, alpha=0.5))
+    torch.cuda.synchronize()
+    pre = c.double() * 0.5 + bias.double()[:, None]
+    want = pre / (1 + torch.exp(-pre))
+    assert ((fused.double() - want).abs() / (want.abs() + 1)).max().item() < 1e-5
+
+
 @pytest.mark.parametrize("dt", [0, 1, 2])
 @pytest.mark.parametrize("m,n,k,splits,kb", SPLITK_CASES)
 def test_splitk_matches_oracle(dt, m, n, k, splits, kb):
