@@ -505,8 +505,9 @@ bool use_pair_kernel(int m, int n, int hint) {
   return m >= 256 && n >= 256;
 }
 
-// Narrow N (33..128 columns) with enough 256-row tiles to occupy most SMs
-// as CTA pairs: the pair kernel with a 64- or 128-wide tile.  Its
+// Narrow N (17..128 columns; 33..128 for fp8) with enough 256-row tiles to
+// occupy most SMs as CTA pairs: the pair kernel with a 32-, 64- or 128-wide
+// tile.  Its
 // cta_group::2 MMAs split B over the two SMs, so each stages half of it, and
 // the ring holds 6-8 stages; the split-K kernel, one SM per 128-row tile,
 // streams a full B per tile and is latency-bound there (W_up, T = 128).
@@ -518,9 +519,15 @@ int narrow_pair_width(const sp24_gemm_desc* d, int sm_count) {
   if (mode == 0) return 0;
   const char* kern = std::getenv("SP24_KERNEL");
   if (kern != nullptr && mode != 1) return 0;   // a forced kernel choice wins
-  if (d->tile_n != 0 || d->n <= 32 || d->n > 128) return 0;
-  const int np = d->n <= 64 ? 64 : 128;
+  if (d->tile_n != 0 || d->n > 128) return 0;
+  // 32-wide tiles stage 16 columns (32 B rows) per CTA: 16-bit types only.
+  if (d->n <= 32 && is_fp8(d->dtype)) return 0;
+  const int np = d->n <= 32 ? 32 : d->n <= 64 ? 64 : 128;
   if (mode == 1) return np;
+  // Up to 16 columns the split-K kernel's 44 KB stages stream A at the HBM
+  // rate; the pair tile wins from 17 columns on (W_up, T = 16: 14.7 us
+  // against 16.4 us; T = 32: 17.1 us against 16.5 us).
+  if (d->n <= 16) return 0;
   const long long pair_tiles =
       static_cast<long long>((d->m + 255) / 256) * ((d->n + np - 1) / np);
   return pair_tiles * 4 >= static_cast<long long>(sm_count / 2) * 3 ? np : 0;
@@ -553,6 +560,9 @@ using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_
 
 template <int DT>
 LaunchFn pick_narrow_pair(int np) {
+  if constexpr (DT != 2) {
+    if (np == 32) return launch_gemm2sm<DT, 0, 32>;
+  }
   return np == 64 ? launch_gemm2sm<DT, 0, 64> : launch_gemm2sm<DT, 0, 128>;
 }
 

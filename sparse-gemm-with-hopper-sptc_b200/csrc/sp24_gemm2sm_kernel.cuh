@@ -71,9 +71,10 @@ struct PairParams {
 // stage and twice as many stages.  A ring slot is freed only when its MMAs
 // complete, so the MMAs queued in the tensor pipe hold part of the ring; finer
 // stages leave more of the same shared memory loading.
-// BNP is the pair tile width: 256 for large N; 128 or 64 for narrow N (an MLP
-// layer applied to 33..128 tokens), where each CTA stages only BNP / 2
-// columns of B, so a stage shrinks to 26-36 KB and the ring holds 6-8 of them.
+// BNP is the pair tile width: 256 for large N; 128, 64 or (16-bit types) 32
+// for narrow N (an MLP layer applied to a few tokens), where each CTA stages
+// only BNP / 2 columns of B, so a stage shrinks to 22-36 KB and the ring
+// holds 6-8 of them.
 template <int DT, int FINE, int BNP = 256>
 struct PairCfg {
   static constexpr int ESZ = (DT == 2) ? 1 : 2;
@@ -112,7 +113,8 @@ struct PairCfg {
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
   static constexpr uint32_t IDESC = make_idesc_sparse(FMT, BNP, 256, true);
-  static_assert(BNP == 64 || BNP == 128 || BNP == 256, "pair tile width 64, 128 or 256");
+  static_assert(BNP == 32 || BNP == 64 || BNP == 128 || BNP == 256,
+                "pair tile width 32, 64, 128 or 256");
   static_assert(B_SPAN >= 32, "B rows of at least 32 bytes per CTA");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
@@ -492,9 +494,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                           static_cast<uint32_t>(half * C::CW);
       uint32_t r[C::CW];
+      if constexpr (C::CW == 16) {
+        tmem_ld_x16(tb, r);
+      } else {
 #pragma unroll
-      for (int c = 0; c < C::CW; c += 32)
-        tmem_ld_x32(tb + static_cast<uint32_t>(c), *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
+        for (int c = 0; c < C::CW; c += 32)
+          tmem_ld_x32(tb + static_cast<uint32_t>(c), *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
+      }
       tmem_ld_wait(r);
       tc_fence_before();
       __syncwarp();
