@@ -297,6 +297,7 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
   P.k_stages = (p.k + bkd - 1) / bkd;
   P.num_tiles = P.m_pairs * P.n_tiles;
   P.group_m = group_m_env(8);
+  P.splits = 1;
   P.c_f32 = p.c_f32;
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
   P.ldc = p.ldc;
@@ -364,25 +365,28 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
 // Largest cluster of split-K CTAs the device keeps resident `tiles` times
 // over (cached per device and split factor).
 std::mutex g_occ_mu;
-int g_occ[kMaxDevices][sp24::kMaxSplits + 1];
+// Per device, kernel family (0 split-K, 1 pair K-split) and cluster size.
+int g_occ[kMaxDevices][2][sp24::kMaxSplits + 1];
 
 template <typename Kern>
-int max_active_clusters(Kern kern, int smem, int splits) {
+int max_active_clusters(Kern kern, int smem, int csize, int family = 0,
+                        unsigned threads = sp24::kThreads) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices ||
+      csize > sp24::kMaxSplits) {
     (void)cudaGetLastError();
     return 0;
   }
   std::lock_guard<std::mutex> lk(g_occ_mu);
-  int& slot = g_occ[dev][splits];
+  int& slot = g_occ[dev][family][csize];
   if (slot == 0) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(splits));
-    cfg.blockDim = dim3(sp24::kThreads);
+    cfg.gridDim = dim3(static_cast<unsigned>(csize));
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
@@ -414,6 +418,48 @@ int choose_splits(Kern kern, int smem, int tiles, int stages, int sm_count) {
   if (forced <= 0)
     while (s > 1 && max_active_clusters(kern, smem, s) < tiles) --s;
   return s;
+}
+
+// The CTA-pair kernel's K-split form: one 256-row tile per cluster of
+// 2 * splits CTAs, pair p summing K slice p (narrow N with few row tiles).
+template <int DT, int BNP>
+sp24_status launch_gemm2sm_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t stream,
+                                  int splits) {
+  using C = sp24::PairCfg<DT, 0, BNP>;
+  auto kern = sp24::sp24_gemm2sm_splitk_kernel<DT, BNP>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    SP24_CUDA_TRY(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    SP24_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    attr_set[dev] = true;
+  }
+  const CUtensorMapDataType tdt =
+      C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUtensorMap ta, tb, te;
+  sp24_status st =
+      encode_2d(&ta, tdt, p.a_c, static_cast<uint64_t>(p.k / 2), static_cast<uint64_t>(p.m),
+                static_cast<uint64_t>(p.lda_c) * C::ESZ, C::A_COLS, sp24::kBlockM,
+                C::A_ROW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st != SP24_OK) return st;
+  st = encode_2d(&tb, tdt, p.b, static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.k),
+                 static_cast<uint64_t>(p.ldb) * C::ESZ, C::B_BOXN, C::BKD,
+                 swizzle_for_span(C::B_SPAN));
+  if (st != SP24_OK) return st;
+  st = encode_meta_rows(&te, p);
+  if (st != SP24_OK) return st;
+  sp24::PairParams P = pair_params(p, C::BKD, 256, BNP);
+  // Every cluster resident at once, at least two stages per slice.
+  splits = std::max(1, std::min(splits, P.k_stages / 2));
+  while (splits > 1 &&
+         max_active_clusters(kern, C::SMEM_BYTES, 2 * splits, 1, sp24::kPairThreads) < P.num_tiles)
+    --splits;
+  P.splits = splits;
+  return launch_gemm_kernel(kern, static_cast<unsigned>(P.num_tiles * 2 * splits),
+                            sp24::kPairThreads, C::SMEM_BYTES, stream,
+                            static_cast<unsigned>(2 * splits), ta, tb, te, P);
 }
 
 template <int DT, int BN, int KB, int G>
@@ -533,6 +579,30 @@ int narrow_pair_width(const sp24_gemm_desc* d, int sm_count) {
   return pair_tiles * 4 >= static_cast<long long>(sm_count / 2) * 3 ? np : 0;
 }
 
+// Narrow N (17..128 columns; 33..128 for fp8) with too few 256-row tiles for
+// the plain pair kernel: its K-split form, S pairs per tile (*splits), so
+// that 2 S CTAs per tile occupy most of the SMs.  Returns the tile width or
+// 0.  SP24_PAIR_SPLITK=0 turns it off; =S forces S pairs on every eligible
+// shape (tests and tuning runs).
+int narrow_pair_splitk_width(const sp24_gemm_desc* d, int sm_count, int* splits) {
+  const char* env = std::getenv("SP24_PAIR_SPLITK");
+  const int forced = env != nullptr ? std::atoi(env) : -1;
+  if (forced == 0) return 0;
+  const char* kern = std::getenv("SP24_KERNEL");
+  if (kern != nullptr && forced < 1) return 0;   // a forced kernel choice wins
+  if (d->tile_n != 0 || d->n > 128 || d->n <= (is_fp8(d->dtype) ? 32 : 16)) return 0;
+  const int np = d->n <= 32 ? 32 : d->n <= 64 ? 64 : 128;
+  if (forced >= 1) {
+    *splits = std::min(forced, 4);
+    return np;
+  }
+  const long long tiles = static_cast<long long>((d->m + 255) / 256) * ((d->n + np - 1) / np);
+  const int s = static_cast<int>(std::min<long long>(4, (sm_count / 2) / std::max(1LL, tiles)));
+  if (s < 2) return 0;
+  *splits = s;
+  return np;
+}
+
 // Tiles at most 128 wide take the split-K kernel when N itself is narrow or
 // the tile count is modest (up to four waves): there its large stages and
 // K splitting win.  With thousands of narrow tiles the persistent
@@ -557,6 +627,16 @@ int splitk_units(int bn) {
 }
 
 using LaunchFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t);
+
+using PairSplitFn = sp24_status (*)(const Prepared&, const DeviceInfo&, cudaStream_t, int);
+
+template <int DT>
+PairSplitFn pick_pair_splitk(int np) {
+  if constexpr (DT != 2) {
+    if (np == 32) return launch_gemm2sm_splitk<DT, 32>;
+  }
+  return np == 64 ? launch_gemm2sm_splitk<DT, 64> : launch_gemm2sm_splitk<DT, 128>;
+}
 
 template <int DT>
 LaunchFn pick_narrow_pair(int np) {
@@ -844,6 +924,13 @@ sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const Devic
                   : d->dtype == SP24_BF16 ? pick_narrow_pair<1>(np)
                                           : pick_narrow_pair<2>(np);
     return nf(p, *di, stream);
+  }
+  int pks = 0;
+  const int npk = narrow_pair_splitk_width(d, di->sm_count, &pks);
+  if (npk > 0) {
+    return d->dtype == SP24_F16    ? pick_pair_splitk<0>(npk)(p, *di, stream, pks)
+           : d->dtype == SP24_BF16 ? pick_pair_splitk<1>(npk)(p, *di, stream, pks)
+                                   : pick_pair_splitk<2>(npk)(p, *di, stream, pks);
   }
   if (use_splitk_kernel(d->m, d->n, bn, di->sm_count)) {
     const int kb = splitk_units(bn);

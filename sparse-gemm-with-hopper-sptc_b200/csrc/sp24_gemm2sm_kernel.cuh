@@ -34,6 +34,7 @@
 #include <cuda_bf16.h>
 
 #include "sp24_gemm_kernel.cuh"
+#include "sp24_gemm_splitk_kernel.cuh"
 #include "sp24_ptx.cuh"
 
 namespace sp24 {
@@ -48,6 +49,7 @@ struct PairParams {
   int m_pairs;    // 256-row tiles
   int n_tiles;    // 256-column tiles
   int k_stages, num_tiles, group_m;
+  int splits;     // K-split form: pairs per cluster (each owns a K slice); 1 otherwise
   float* c_f32;
   __nv_bfloat16* c_bf16;
   long long ldc;
@@ -103,6 +105,7 @@ struct PairCfg {
   static constexpr uint32_t B_SBO = 8 * B_SPAN;                 // 8-row K group stride
   static constexpr int B_MMA_ADVANCE = MMA_K * B_SPAN;
   static constexpr int CW = BNP / 2;                            // columns per epilogue warp
+  static constexpr int RS = BNP + 4;                            // parked partial row stride
   static constexpr int E_BYTES = E_PER * kAtomBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
   static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
@@ -118,6 +121,7 @@ struct PairCfg {
   static_assert(B_SPAN >= 32, "B rows of at least 32 bytes per CTA");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
+  static_assert(kBlockM * RS * 4 <= STAGES * STAGE_BYTES, "a parked partial tile fits the ring");
   static_assert(LOADS <= 32, "one lane per TMA box");
 };
 
@@ -260,13 +264,18 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
   }
 }
 
-template <int DT, int FINE, int BNP>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
-    sp24_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmE, const PairParams P) {
+// The kernel body.  KS = 0: clusters of 2, persistent over the tiles.
+// KS = 1 (K-split form, for too few 256-row tiles to occupy the GPU): a
+// cluster of 2 S CTAs computes one tile; pair p (CTAs 2p, 2p+1) accumulates
+// K slice p in its TMEM, parks its fp32 partial tile in its idle ring, and
+// after a cluster barrier each CTA sums its share of rows over all S pairs
+// through distributed shared memory (fixed order) and stores them.
+template <int DT, int FINE, int BNP, int KS>
+SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
+                             const CUtensorMap& tmE, const PairParams& P) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using C = PairCfg<DT, FINE, BNP>;
+  static_assert(!KS || FINE == 0, "K slices start on whole metadata atoms");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -281,9 +290,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1;
-  const int npairs = gridDim.x >> 1;
+  const uint32_t lead = KS ? (rank & ~1u) : 0u;   // cluster rank of this pair's leader
+  const uint32_t prank = rank - lead;             // 0 or 1 inside the pair
+  const bool leader = prank == 0;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << lead);
+  const int pair = KS ? static_cast<int>(blockIdx.x) / (2 * P.splits)
+                      : static_cast<int>(blockIdx.x >> 1);
+  const int npairs = KS ? P.num_tiles : static_cast<int>(gridDim.x >> 1);   // KS: one tile
+  const int split = KS ? static_cast<int>(rank >> 1) : 0;
+  const int kst0 = KS ? P.k_stages * split / P.splits : 0;          // this pair's K slice
+  const int kst1 = KS ? P.k_stages * (split + 1) / P.splits : P.k_stages;
 
   if (threadIdx.x == 0) {
     abort_sh = 0;
@@ -333,7 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // leader's full barrier, which each leader warp arms with its share.
     if (!P.stall_producer) {
       const bool is_b = warp == kPairBWarp;
-      const uint32_t full0_leader = mapa_shared(smem_u32(&full_bar[0]), 0);
+      const uint32_t full0_leader = mapa_shared(smem_u32(&full_bar[0]), lead);
       const CUtensorMap* lane_map = is_b ? &tmB : (lane == 0 ? &tmA : &tmE);
       const uint32_t lane_off =
           is_b ? static_cast<uint32_t>(C::A_BYTES + lane * C::B_BOX_BYTES)
@@ -354,11 +370,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       for (int t = pair; t < P.num_tiles && ok; t += npairs) {
         int mp, nb;
         pair_tile_coords(P, t, mp, nb);
-        const int row0 = mp * 256 + static_cast<int>(rank) * 128;
-        const int mb = mp * 2 + static_cast<int>(rank);
-        int x = is_b ? nb * C::BN + static_cast<int>(rank) * C::BN_CTA + lane * C::B_BOXN : 0;
+        const int row0 = mp * 256 + static_cast<int>(prank) * 128;
+        const int mb = mp * 2 + static_cast<int>(prank);
+        int x = is_b ? nb * C::BN + static_cast<int>(prank) * C::BN_CTA + lane * C::B_BOXN : 0;
         int y = is_b ? 0 : (lane == 0 ? row0 : ((lane - 1) * P.m_blocks + mb) * 8);
-        for (int ks = 0; ks < P.k_stages; ++ks) {
+        x += kst0 * dx;
+        y += kst0 * dy;
+        for (int ks = kst0; ks < kst1; ++ks) {
           int good = 1;
           if (lane == 0) good = mbar_wait_fast(&empty_bar[s], ph ^ 1u, &abort_sh, tmo) ? 1 : 0;
           if (__shfl_sync(0xffffffffu, good, 0) == 0) {
@@ -429,7 +447,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           break;
         }
         tc_fence_after();
-        for (int ks = 0; ks < P.k_stages; ++ks) {
+        for (int ks = kst0; ks < kst1; ++ks) {
           if (!mbar_wait_warp(&full_bar[s], ph, &abort_sh, tmo)) {
             ok = false;
             break;
@@ -442,7 +460,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           if (sub == 0) ebuf ^= static_cast<uint32_t>(C::E_PER * 4);
           const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
           const int kleft = P.k - ks * C::BKD;
-          const uint32_t acc0 = ks > 0 ? 1u : 0u;
+          const uint32_t acc0 = ks > kst0 ? 1u : 0u;
           if (elect_one()) {
             if (sub == 0) {
 #pragma unroll
@@ -457,7 +475,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                    e_tmem + (C::SPA == 1 ? ecol[0][j] : ecol[sub & (C::SPA - 1)][j]),
                                    C::SPA == 1 ? isel[0][j] : isel[sub & (C::SPA - 1)][j],
                                    j > 0 ? 1u : acc0);
-            tc_commit_to<2>(&empty_bar[s], static_cast<uint16_t>(3));
+            tc_commit_to<2>(&empty_bar[s], pair_mask);
           }
           __syncwarp();
           any = true;
@@ -465,13 +483,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           if (++s == C::STAGES) s = 0, ph ^= 1u, soff = 0;
         }
         if (!ok) break;
-        if (elect_one()) tc_commit_to<2>(&accf_bar, static_cast<uint16_t>(3));
+        if (elect_one()) tc_commit_to<2>(&accf_bar, pair_mask);
         __syncwarp();
         aph ^= 1u;
       }
       if (!ok && any) {
         volatile int dummy = 0;
-        if (elect_one()) tc_commit_to<2>(&drain_bar, static_cast<uint16_t>(1));
+        if (elect_one()) tc_commit_to<2>(&drain_bar, static_cast<uint16_t>(1u << lead));
         __syncwarp();
         if (lane == 0) mbar_wait(&drain_bar, 0, &dummy, tmo);
         __syncwarp();
@@ -481,7 +499,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    const uint32_t acce_leader = mapa_shared(smem_u32(&acce_bar), 0);
+    const uint32_t acce_leader = mapa_shared(smem_u32(&acce_bar), lead);
     uint32_t aph = 0;
     for (int t = pair; t < P.num_tiles; t += npairs) {
       int mp, nb;
@@ -504,24 +522,95 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       tmem_ld_wait(r);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acce_leader);
-      const int row = mp * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
-      pair_store_row<C::CW>(P, r, row, nb * C::BN + half * C::CW);
-      if (P.peers.n > 0) pair_push_rows_to_peers<C::CW>(P, row - lane, nb * C::BN + half * C::CW);
+      if constexpr (KS) {
+        // K slice done: park the raw partial sums in the idle ring.
+        float* red = reinterpret_cast<float*>(smem);
+        const int rl = q * 32 + lane;
+#pragma unroll
+        for (int c = 0; c < C::CW; c += 4)
+          *reinterpret_cast<float4*>(red + rl * C::RS + half * C::CW + c) =
+              make_float4(__uint_as_float(r[c]), __uint_as_float(r[c + 1]),
+                          __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+      } else {
+        if (lane == 0) mbar_arrive_cluster(acce_leader);
+        const int row = mp * 256 + static_cast<int>(prank) * 128 + q * 32 + lane;
+        pair_store_row<C::CW>(P, r, row, nb * C::BN + half * C::CW);
+        if (P.peers.n > 0)
+          pair_push_rows_to_peers<C::CW>(P, row - lane, nb * C::BN + half * C::CW);
+      }
       aph ^= 1u;
     }
   }
 
-  if (P.peers.n > 0) __threadfence_system();   // peer stores visible before completion
   tc_fence_before();
   __syncthreads();
-  cluster_sync();
+  cluster_sync();   // KS: every pair's partial is parked and visible (release/acquire)
+  if constexpr (KS) {
+    // CTA (slice p, pair rank pr) finishes rows [128 p / S, 128 (p+1) / S)
+    // of its half of the tile: partials of the S pairs summed in slice order.
+    int mp, nb;
+    pair_tile_coords(P, pair, mp, nb);
+    const int S = P.splits;
+    const int r0 = kBlockM * split / S;
+    const int r1 = kBlockM * (split + 1) / S;
+    constexpr int NV = C::BN / 4;
+    const float* red = reinterpret_cast<const float*>(smem);
+    for (int idx = threadIdx.x; idx < (r1 - r0) * NV; idx += kPairThreads) {
+      const int rl = r0 + idx / NV;
+      const int cg = idx - (idx / NV) * NV;
+      const uint32_t la = smem_u32(red + rl * C::RS + cg * 4);
+      float4 acc = ld_dsmem_f4(mapa_shared(la, prank));
+      for (int sp = 1; sp < S; ++sp) {
+        const float4 v = ld_dsmem_f4(mapa_shared(la, 2u * static_cast<uint32_t>(sp) + prank));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int row = mp * 256 + static_cast<int>(prank) * 128 + rl;
+      if (row >= P.m) continue;
+      const bool hb = P.bias != nullptr;
+      const float b = hb ? P.bias[row] : 0.0f;
+      float4 o = make_float4(epi_value(acc.x, P.alpha, b, hb, P.act),
+                             epi_value(acc.y, P.alpha, b, hb, P.act),
+                             epi_value(acc.z, P.alpha, b, hb, P.act),
+                             epi_value(acc.w, P.alpha, b, hb, P.act));
+      const int col = nb * C::BN + cg * 4;
+      if (P.gate_from_c) {
+        if (col + 0 < P.n) o.x *= load_c(P, row, col + 0);
+        if (col + 1 < P.n) o.y *= load_c(P, row, col + 1);
+        if (col + 2 < P.n) o.z *= load_c(P, row, col + 2);
+        if (col + 3 < P.n) o.w *= load_c(P, row, col + 3);
+      }
+      store_vec4(P, o, row, col);
+    }
+    // No CTA leaves (releasing its shared memory) while others still read it.
+    cluster_sync();
+  }
+  if (P.peers.n > 0) __threadfence_system();   // peer stores visible before completion
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && abort_sh != 0 && P.status != nullptr) atomicExch(P.status, 1);
 #endif
+}
+
+template <int DT, int FINE, int BNP>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    sp24_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmE, const PairParams P) {
+  pair_gemm_body<DT, FINE, BNP, 0>(tmA, tmB, tmE, P);
+}
+
+// K-split form: launched with a run-time cluster of 2 * P.splits CTAs.
+template <int DT, int BNP>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    sp24_gemm2sm_splitk_kernel(const __grid_constant__ CUtensorMap tmA,
+                               const __grid_constant__ CUtensorMap tmB,
+                               const __grid_constant__ CUtensorMap tmE, const PairParams P) {
+  pair_gemm_body<DT, 0, BNP, 1>(tmA, tmB, tmE, P);
 }
 
 }  // namespace sp24

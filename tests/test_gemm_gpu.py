@@ -306,6 +306,66 @@ def test_narrow_pair_matches_oracle(dt, m, n, k):
     assert (c - c_split).abs().max().item() <= 1e-5 * scale
 
 
+PAIR_SPLIT_CASES = [
+    # m, n, k, pairs per tile: whole and ragged M, 32/64/128-wide tiles, K
+    # slices of unequal length, a K too short for the requested split
+    (512, 64, 4096, "4"), (640, 128, 2048, "2"), (1000, 100, 1536, "4"), (256, 24, 8192, "3"),
+    (768, 48, 640, "4"), (256, 128, 256, "4"),
+]
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k,splits", PAIR_SPLIT_CASES)
+def test_pair_splitk_matches_oracle(dt, m, n, k, splits):
+    """The CTA-pair kernel's K-split form (a cluster of 2 S CTAs per tile,
+    partial tiles reduced over distributed shared memory): within the
+    row-norm bound of the oracle, bf16 output the rounding of the fp32
+    output, a repeat call bit-identical, and within fp32 rounding of the
+    unsplit pair tile."""
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    if dt == 2 and n <= 32:
+        pytest.skip("32-wide pair tiles are 16-bit only")
+    gen = oracle.Gen(m + 19 * n + k)
+    a, b, _, _, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    b_t = to_dev(b, dt)
+
+    def run():
+        return sp24.gemm(ac_t, e_t, b_t, m, n, k, out_bf16=True, dtype=lib_dtype(dt))
+
+    env = {"SP24_PAIR_SPLITK": splits, "SP24_NARROW_PAIR": "0"}
+    c, cb = _with_env(env, run)
+    c_again, _ = _with_env(env, run)
+    c_one, _ = _with_env({"SP24_NARROW_PAIR": "1"}, run)
+    torch.cuda.synchronize()
+    check_c(c, c_ref, a, b, dt, abs_rule=(k <= 1024))
+    assert torch.equal(cb, c.to(torch.bfloat16))
+    assert torch.equal(c, c_again)
+    scale = c_one.abs().max().item() + 1.0
+    assert (c - c_one).abs().max().item() <= 1e-5 * scale
+
+
+def test_pair_splitk_epilogue():
+    """alpha, per-row bias and SiLU applied once, after the slices are summed."""
+    m, n, k = 640, 128, 4096
+    gen = oracle.Gen(5)
+    a, b, *_ = oracle.host_case(gen, 1, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, 1))
+    img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
+    b_t = to_dev(b, 1)
+    bias = torch.linspace(-2, 2, m, device=DEV)
+    env = {"SP24_PAIR_SPLITK": "4", "SP24_NARROW_PAIR": "0"}
+    fused, _ = _with_env(env, lambda: sp24.gemm_fused(ac_t, img, b_t, m, n, k, bias=bias,
+                                                      act=sp24.ACT_SILU, alpha=0.25))
+    plain, _ = _with_env(env, lambda: sp24.gemm(ac_t, img, b_t, m, n, k,
+                                                meta_format=sp24.META_TC))
+    torch.cuda.synchronize()
+    pre = plain.double() * 0.25 + bias.double()[:, None]
+    want = pre / (1 + torch.exp(-pre))
+    assert ((fused.double() - want).abs() / (want.abs() + 1)).max().item() < 1e-5
+
+
 @pytest.mark.parametrize("n", [16, 32, 64, 128])
 def test_narrow_pair_decode_and_epilogue(n):
     """B = identity through the narrow pair tile gives A exactly; bias and
