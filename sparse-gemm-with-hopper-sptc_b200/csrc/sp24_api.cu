@@ -880,17 +880,31 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   if (p.a_c_up != nullptr) {
     const int bn = std::min(128, choose_bn(d->m, d->n, d->tile_n, di->sm_count));
     const long long tiles = static_cast<long long>((d->m + 127) / 128) * ((d->n + bn - 1) / bn);
-    if (d->n <= 128 || tiles <= 4LL * di->sm_count) {
+    // Up to 64 columns, and for wider N while the tile count is modest, both
+    // weights stream through one split-K launch.  From 65 columns on, where
+    // the narrow dispatch runs CTA pairs, two pair launches beat it (W_up
+    // shapes, T = 128: 42.7 us against 46.9 us; at T = 64 one launch still
+    // wins, 33.7 us against 36.1 us).  SP24_GATED=1|2 forces one or two
+    // launches.
+    int pks = 0;
+    const bool pairs_narrow = d->n > 64 && d->n <= 128 &&
+                              (narrow_pair_width(d, di->sm_count) > 0 ||
+                               narrow_pair_splitk_width(d, di->sm_count, &pks) > 0);
+    const char* genv = std::getenv("SP24_GATED");
+    const int gmode = genv != nullptr ? std::atoi(genv) : 0;
+    const bool one_launch = gmode == 1 || (gmode != 2 && !pairs_narrow &&
+                                           (d->n <= 128 || tiles <= 4LL * di->sm_count));
+    if (one_launch) {
       // One launch: both weights through the split-K kernel's ring.
       LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)
                     : d->dtype == SP24_BF16 ? pick_gated<1>(bn)
                                             : pick_gated<2>(bn);
       return gf(p, *di, stream);
     }
-    // Wide N (compute-bound): two passes on the regular kernels with C as the
-    // intermediate.  Pass 1 writes act(alpha W_gate B + bias) into C (fp32
-    // when the caller asked for it, else bf16); pass 2 multiplies
-    // (alpha_up W_up B + bias_up) by it in its epilogue and writes the result.
+    // Two passes on the regular kernels with C as the intermediate.  Pass 1
+    // writes act(alpha W_gate B + bias) into C (fp32 when the caller asked
+    // for it, else bf16); pass 2 multiplies (alpha_up W_up B + bias_up) by it
+    // in its epilogue and writes the result.
     Prepared p1 = p;
     p1.a_c_up = nullptr;
     if (p1.c_f32 != nullptr) p1.c_bf16 = nullptr;
