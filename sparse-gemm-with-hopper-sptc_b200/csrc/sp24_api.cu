@@ -591,7 +591,10 @@ int narrow_pair_splitk_width(const sp24_gemm_desc* d, int sm_count, int* splits)
   const char* kern = std::getenv("SP24_KERNEL");
   if (kern != nullptr && forced < 1) return 0;   // a forced kernel choice wins
   if (d->tile_n != 0 || d->n > 128 || d->n <= (is_fp8(d->dtype) ? 32 : 16)) return 0;
-  const int np = d->n <= 32 ? 32 : d->n <= 64 ? 64 : 128;
+  int np = d->n <= 32 ? 32 : d->n <= 64 ? 64 : 128;
+  const char* wenv = std::getenv("SP24_PAIR_SPLITK_WIDTH");   // tuning: 64 or 128
+  if (wenv != nullptr && (std::atoi(wenv) == 64 || std::atoi(wenv) == 128) && d->n > 32)
+    np = std::atoi(wenv);
   if (forced >= 1) {
     *splits = std::min(forced, 4);
     return np;
