@@ -305,6 +305,8 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
   P.idesc_ab = p.idesc_ab;
   P.bias = p.bias;
   P.act = p.act;
+  P.alpha_up = p.alpha_up;
+  P.bias_up = p.bias_up;
   P.gate_from_c = p.gate_from_c;
   P.peers = p.peers;
   P.vec_f32 = p.c_f32 == nullptr                            ? 0
@@ -322,16 +324,16 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
 }
 
 // Metadata image viewed as rows of 256 B: one 2 KB atom = an 8-row box.
-sp24_status encode_meta_rows(CUtensorMap* te, const Prepared& p) {
+sp24_status encode_meta_rows(CUtensorMap* te, const Prepared& p, const uint8_t* image = nullptr) {
   const uint64_t lanes = static_cast<uint64_t>(meta_katoms(p.k)) * meta_mblocks(p.m) * 128;
-  return encode_2d(te, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.meta_tc, 256, lanes * 16 / 256, 256, 256,
-                   8, CU_TENSOR_MAP_SWIZZLE_NONE);
+  return encode_2d(te, CU_TENSOR_MAP_DATA_TYPE_UINT8, image != nullptr ? image : p.meta_tc, 256,
+                   lanes * 16 / 256, 256, 256, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-template <int DT, int FINE, int BNP = 256>
+template <int DT, int FINE, int BNP = 256, int G = 1>
 sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
-  using C = sp24::PairCfg<DT, FINE, BNP>;
-  auto kern = sp24::sp24_gemm2sm_kernel<DT, FINE, BNP>;
+  using C = sp24::PairCfg<DT, FINE, BNP, G>;
+  auto kern = sp24::sp24_gemm2sm_kernel<DT, FINE, BNP, G>;
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   SP24_CUDA_TRY(cudaGetDevice(&dev));
@@ -354,12 +356,21 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   if (st != SP24_OK) return st;
   st = encode_meta_rows(&te, p);
   if (st != SP24_OK) return st;
+  CUtensorMap ta2 = ta, te2 = te;
+  if constexpr (G == 2) {   // W_up of the gated form
+    st = encode_2d(&ta2, tdt, p.a_c_up, static_cast<uint64_t>(p.k / 2), static_cast<uint64_t>(p.m),
+                   static_cast<uint64_t>(p.lda_c_up) * C::ESZ, C::A_COLS, sp24::kBlockM,
+                   C::A_ROW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st != SP24_OK) return st;
+    st = encode_meta_rows(&te2, p, p.meta_up);
+    if (st != SP24_OK) return st;
+  }
 
   const sp24::PairParams P = pair_params(p, C::BKD, 256, BNP);
   const int pairs = std::max(1, std::min(P.num_tiles, di.sm_count / 2));
   // Cluster shape (2) comes from the kernel's __cluster_dims__.
   return launch_gemm_kernel(kern, static_cast<unsigned>(2 * pairs), sp24::kPairThreads,
-                            C::SMEM_BYTES, stream, 0, ta, tb, te, P);
+                            C::SMEM_BYTES, stream, 0, ta, tb, te, ta2, te2, P);
 }
 
 // Largest cluster of split-K CTAs the device keeps resident `tiles` times
@@ -642,6 +653,11 @@ PairSplitFn pick_pair_splitk(int np) {
 }
 
 template <int DT>
+LaunchFn pick_pair_gated(int np) {
+  return np == 64 ? launch_gemm2sm<DT, 0, 64, 2> : launch_gemm2sm<DT, 0, 128, 2>;
+}
+
+template <int DT>
 LaunchFn pick_narrow_pair(int np) {
   if constexpr (DT != 2) {
     if (np == 32) return launch_gemm2sm<DT, 0, 32>;
@@ -897,6 +913,15 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     const int gmode = genv != nullptr ? std::atoi(genv) : 0;
     const bool one_launch = gmode == 1 || (gmode != 2 && !pairs_narrow &&
                                            (d->n <= 128 || tiles <= 4LL * di->sm_count));
+    const int npg = narrow_pair_width(d, di->sm_count);
+    if (gmode != 1 && gmode != 2 && npg >= 64 && d->n > 32 &&
+        std::getenv("SP24_PAIR_GATED") == nullptr) {
+      // One launch on CTA pairs: W_gate and W_up against the same B stages.
+      LaunchFn pg = d->dtype == SP24_F16    ? pick_pair_gated<0>(npg)
+                    : d->dtype == SP24_BF16 ? pick_pair_gated<1>(npg)
+                                            : pick_pair_gated<2>(npg);
+      return pg(p, *di, stream);
+    }
     if (one_launch) {
       // One launch: both weights through the split-K kernel's ring.
       LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)

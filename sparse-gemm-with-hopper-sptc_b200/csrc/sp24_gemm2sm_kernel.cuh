@@ -58,6 +58,8 @@ struct PairParams {
   float alpha;
   const float* bias;  // optional per-row bias (m floats)
   int act;            // kActNone / kActSilu
+  float alpha_up;         // gated form (G = 2): W_up's scale and optional bias
+  const float* bias_up;
   int gate_from_c;    // second pass of a two-pass gated epilogue: multiply by the value
                       // already in C (c_f32 if given, else c_bf16) before storing
   int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
@@ -77,7 +79,10 @@ struct PairParams {
 // for narrow N (an MLP layer applied to a few tokens), where each CTA stages
 // only BNP / 2 columns of B, so a stage shrinks to 22-36 KB and the ring
 // holds 6-8 of them.
-template <int DT, int FINE, int BNP = 256>
+// G = 2 is the gated form (SwiGLU, narrow tiles only): W_gate and W_up stream
+// through one ring against the same B stages into two accumulators, and the
+// epilogue writes act(alpha W_gate B + b) * (alpha_up W_up B + b_up).
+template <int DT, int FINE, int BNP = 256, int G = 1>
 struct PairCfg {
   static constexpr int ESZ = (DT == 2) ? 1 : 2;
   static constexpr int KIND = (DT == 2) ? 1 : 0;
@@ -88,7 +93,8 @@ struct PairCfg {
   static constexpr int SPA = BKD >= 128 ? 1 : 128 / BKD;        // stages sharing one atom
   static constexpr int A_ROW = BKD / 2 * ESZ;                   // bytes of a compressed A row
   static constexpr int A_COLS = A_ROW / ESZ;
-  static constexpr int A_BYTES = kBlockM * A_ROW;
+  static constexpr int A_ONE = kBlockM * A_ROW;                 // one weight's A_c box
+  static constexpr int A_BYTES = G * A_ONE;
   static constexpr uint32_t A_LAYOUT = A_ROW == 128 ? kLayoutSW128 : kLayoutSW64;
   static constexpr uint32_t A_SBO = 8 * A_ROW;                  // 8-row group stride
   static constexpr int BN = BNP;                                // pair tile width
@@ -106,12 +112,12 @@ struct PairCfg {
   static constexpr int B_MMA_ADVANCE = MMA_K * B_SPAN;
   static constexpr int CW = BNP / 2;                            // columns per epilogue warp
   static constexpr int RS = BNP + 4;                            // parked partial row stride
-  static constexpr int E_BYTES = E_PER * kAtomBytes;
+  static constexpr int E_BYTES = G * E_PER * kAtomBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + E_BYTES;
   static constexpr int STAGES_RAW = (kSmemBudget - 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-  static constexpr int LOADS = 1 + B_BOXES + E_PER;             // TMA boxes per stage per CTA
+  static constexpr int LOADS = G + B_BOXES + G * E_PER;         // TMA boxes per stage per CTA
   static constexpr int E_COL = 256;                             // two buffers of E_PER*4 columns
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
@@ -123,6 +129,8 @@ struct PairCfg {
   static_assert(STAGES >= 3, "pair kernel wants a deep ring");
   static_assert(kBlockM * RS * 4 <= STAGES * STAGE_BYTES, "a parked partial tile fits the ring");
   static_assert(LOADS <= 32, "one lane per TMA box");
+  static_assert(G == 1 || (FINE == 0 && BNP >= 64 && G * BNP <= 256),
+                "gated form: coarse stages, 64- or 128-wide tiles");
 };
 
 SP24_DEV void pair_tile_coords(const PairParams& P, int t, int& mp, int& nb) {
@@ -270,12 +278,14 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
 // K slice p in its TMEM, parks its fp32 partial tile in its idle ring, and
 // after a cluster barrier each CTA sums its share of rows over all S pairs
 // through distributed shared memory (fixed order) and stores them.
-template <int DT, int FINE, int BNP, int KS>
+template <int DT, int FINE, int BNP, int KS, int G>
 SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
-                             const CUtensorMap& tmE, const PairParams& P) {
+                             const CUtensorMap& tmE, const CUtensorMap& tmA2,
+                             const CUtensorMap& tmE2, const PairParams& P) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using C = PairCfg<DT, FINE, BNP>;
+  using C = PairCfg<DT, FINE, BNP, G>;
   static_assert(!KS || FINE == 0, "K slices start on whole metadata atoms");
+  static_assert(!KS || G == 1, "the K-split form is ungated");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -324,6 +334,10 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmE);
+    if constexpr (G == 2) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmE2);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(&tmem_base_sh, C::TMEM_COLS);
@@ -348,20 +362,26 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
     // constant step per stage.  Completion bytes of both CTAs land on the
     // leader's full barrier, which each leader warp arms with its share.
     if (!P.stall_producer) {
+      // Warp 0: lanes 0..G-1 the A_c box of each weight, then the metadata
+      // atoms (weight-major); warp 10: the B boxes.
       const bool is_b = warp == kPairBWarp;
+      const bool is_a = !is_b && lane < G;
+      const int el = lane - G;                                 // metadata lane index
+      const int ew = el >= C::E_PER ? 1 : 0;                   // its weight (gated form)
       const uint32_t full0_leader = mapa_shared(smem_u32(&full_bar[0]), lead);
-      const CUtensorMap* lane_map = is_b ? &tmB : (lane == 0 ? &tmA : &tmE);
+      const CUtensorMap* lane_map = is_b ? &tmB
+                                    : is_a ? (lane == 1 ? &tmA2 : &tmA)
+                                           : (ew == 1 ? &tmE2 : &tmE);
       const uint32_t lane_off =
           is_b ? static_cast<uint32_t>(C::A_BYTES + lane * C::B_BOX_BYTES)
-               : (lane == 0 ? 0u
-                            : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES +
-                                                    (lane - 1) * kAtomBytes));
-      const int lanes_e = is_b ? C::B_BOXES : 1 + C::E_PER;  // stages that carry metadata
-      const int lanes_n = is_b ? C::B_BOXES : 1;             // stages that do not
+               : (is_a ? static_cast<uint32_t>(lane * C::A_ONE)
+                       : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + el * kAtomBytes));
+      const int lanes_e = is_b ? C::B_BOXES : G + G * C::E_PER;  // stages that carry metadata
+      const int lanes_n = is_b ? C::B_BOXES : G;                 // stages that do not
       const uint32_t tx_e = 2u * (is_b ? C::B_BYTES : C::A_BYTES + C::E_BYTES);
       const uint32_t tx_n = 2u * (is_b ? C::B_BYTES : C::A_BYTES);
-      const int dx = (!is_b && lane == 0) ? C::A_COLS : 0;
-      const int dy = is_b ? C::BKD : (lane == 0 ? 0 : C::E_PER * P.m_blocks * 8 / C::SPA);
+      const int dx = is_a ? C::A_COLS : 0;
+      const int dy = is_b ? C::BKD : (is_a ? 0 : C::E_PER * P.m_blocks * 8 / C::SPA);
       int s = 0;
       uint32_t ph = 0;
       uint32_t soff = 0;
@@ -373,7 +393,7 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
         const int row0 = mp * 256 + static_cast<int>(prank) * 128;
         const int mb = mp * 2 + static_cast<int>(prank);
         int x = is_b ? nb * C::BN + static_cast<int>(prank) * C::BN_CTA + lane * C::B_BOXN : 0;
-        int y = is_b ? 0 : (lane == 0 ? row0 : ((lane - 1) * P.m_blocks + mb) * 8);
+        int y = is_b ? 0 : (is_a ? row0 : ((el - ew * C::E_PER) * P.m_blocks + mb) * 8);
         x += kst0 * dx;
         y += kst0 * dy;
         for (int ks = kst0; ks < kst1; ++ks) {
@@ -457,24 +477,28 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
           }
           tc_fence_after();
           const int sub = ks % C::SPA;
-          if (sub == 0) ebuf ^= static_cast<uint32_t>(C::E_PER * 4);
+          if (sub == 0) ebuf ^= static_cast<uint32_t>(G * C::E_PER * 4);
           const uint32_t e_tmem = tmem_base + static_cast<uint32_t>(C::E_COL) + ebuf;
           const int kleft = P.k - ks * C::BKD;
           const uint32_t acc0 = ks > kst0 ? 1u : 0u;
           if (elect_one()) {
             if (sub == 0) {
 #pragma unroll
-              for (int a = 0; a < C::E_PER; ++a)
+              for (int a = 0; a < G * C::E_PER; ++a)
                 tc_cp<2>(e_tmem + 4 * a, edesc0 + soff + a * (kAtomBytes >> 4));
             }
 #pragma unroll
-            for (int j = 0; j < C::MMAS; ++j)
-              if (j * C::MMA_K < kleft)
-                tc_mma<2, C::KIND>(tmem_base, adesc0 + soff + j * 2,
-                                   bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4),
-                                   e_tmem + (C::SPA == 1 ? ecol[0][j] : ecol[sub & (C::SPA - 1)][j]),
-                                   C::SPA == 1 ? isel[0][j] : isel[sub & (C::SPA - 1)][j],
-                                   j > 0 ? 1u : acc0);
+            for (int w = 0; w < G; ++w)
+#pragma unroll
+              for (int j = 0; j < C::MMAS; ++j)
+                if (j * C::MMA_K < kleft)
+                  tc_mma<2, C::KIND>(
+                      tmem_base + static_cast<uint32_t>(w * BNP),
+                      adesc0 + soff + w * (C::A_ONE >> 4) + j * 2,
+                      bdesc0 + soff + j * (C::B_MMA_ADVANCE >> 4),
+                      e_tmem + 4u * static_cast<uint32_t>(w * C::E_PER) +
+                          (C::SPA == 1 ? ecol[0][j] : ecol[sub & (C::SPA - 1)][j]),
+                      C::SPA == 1 ? isel[0][j] : isel[sub & (C::SPA - 1)][j], j > 0 ? 1u : acc0);
             tc_commit_to<2>(&empty_bar[s], pair_mask);
           }
           __syncwarp();
@@ -520,6 +544,30 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
           tmem_ld_x32(tb + static_cast<uint32_t>(c), *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
       }
       tmem_ld_wait(r);
+      if constexpr (G == 2) {
+        // Gated form: W_up's accumulator sits BNP columns further on.
+        uint32_t ru[C::CW];
+#pragma unroll
+        for (int c = 0; c < C::CW; c += 32)
+          tmem_ld_x32(tb + static_cast<uint32_t>(BNP + c), *reinterpret_cast<uint32_t(*)[32]>(&ru[c]));
+        tmem_ld_wait(ru);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acce_leader);
+        const int row = mp * 256 + static_cast<int>(prank) * 128 + q * 32 + lane;
+        if (row < P.m) {
+          const bool hg = P.bias != nullptr, hu = P.bias_up != nullptr;
+          const float bg = hg ? P.bias[row] : 0.0f, bu = hu ? P.bias_up[row] : 0.0f;
+#pragma unroll
+          for (int c = 0; c < C::CW; ++c)
+            r[c] = __float_as_uint(
+                epi_value(__uint_as_float(r[c]), P.alpha, bg, hg, P.act) *
+                epi_value(__uint_as_float(ru[c]), P.alpha_up, bu, hu, kActNone));
+          pair_store_row_to<C::CW>(P, P.c_f32, P.c_bf16, r, row, nb * C::BN + half * C::CW);
+        }
+        aph ^= 1u;
+        continue;
+      }
       tc_fence_before();
       __syncwarp();
       if constexpr (KS) {
@@ -596,12 +644,16 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
 #endif
 }
 
-template <int DT, int FINE, int BNP>
+// tmA2 / tmE2: W_up's A_c and metadata maps (gated form); the plain form
+// passes tmA / tmE again.
+template <int DT, int FINE, int BNP, int G>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     sp24_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmE, const PairParams P) {
-  pair_gemm_body<DT, FINE, BNP, 0>(tmA, tmB, tmE, P);
+                        const __grid_constant__ CUtensorMap tmE,
+                        const __grid_constant__ CUtensorMap tmA2,
+                        const __grid_constant__ CUtensorMap tmE2, const PairParams P) {
+  pair_gemm_body<DT, FINE, BNP, 0, G>(tmA, tmB, tmE, tmA2, tmE2, P);
 }
 
 // K-split form: launched with a run-time cluster of 2 * P.splits CTAs.
@@ -610,7 +662,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     sp24_gemm2sm_splitk_kernel(const __grid_constant__ CUtensorMap tmA,
                                const __grid_constant__ CUtensorMap tmB,
                                const __grid_constant__ CUtensorMap tmE, const PairParams P) {
-  pair_gemm_body<DT, 0, BNP, 1>(tmA, tmB, tmE, P);
+  pair_gemm_body<DT, 0, BNP, 1, 1>(tmA, tmB, tmE, tmA, tmE, P);
 }
 
 }  // namespace sp24

@@ -712,6 +712,10 @@ def test_gated_silu_mlp(m, n, k, splits, dt):
     """SwiGLU in one launch: silu(alpha W_gate B + b_g) * (alpha_up W_up B + b_u)
     against the same composition of two plain GEMMs (fp32 on the host), and
     against the oracle's fp32 GEMMs with a bound scaled by both factors."""
+    _gated_check(m, n, k, dt, {"SP24_SPLITS": splits} if splits else {})
+
+
+def _gated_check(m, n, k, dt, env):
     gen = oracle.Gen(m * 3 + n + dt)
     wg, b, _, _, g_ref = oracle.host_case(gen, dt, m, n, k, False)
     wu, _, _, _, _ = oracle.host_case(gen, dt, m, n, k, False)
@@ -724,7 +728,6 @@ def test_gated_silu_mlp(m, n, k, splits, dt):
     rng = np.random.default_rng(n)
     bg = torch.from_numpy(rng.uniform(-1, 1, m).astype(np.float32)).to(DEV)
     bu = torch.from_numpy(rng.uniform(-1, 1, m).astype(np.float32)).to(DEV)
-    env = {"SP24_SPLITS": splits} if splits else {}
 
     def run():
         out, out16 = sp24.gemm_fused(acg, img_g, b_t, m, n, k, bias=bg, act=sp24.ACT_SILU,
@@ -749,6 +752,15 @@ def test_gated_silu_mlp(m, n, k, splits, dt):
     rowscale = np.outer(np.linalg.norm(af, axis=1), np.linalg.norm(bf, axis=0)) / np.sqrt(k)
     bound = rowscale * (2.0 * (np.abs(ur) + 1) + 0.5 * (np.abs(_silu(gr)) + 1))
     assert (np.abs(out.cpu().numpy() - ref) / bound).max() <= TOL[dt]
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 64, 2048), (768, 128, 1024), (1000, 100, 512)])
+@pytest.mark.parametrize("dt", [1, 2])
+def test_gated_silu_mlp_pair_form(m, n, k, dt):
+    """The gated form of the CTA-pair kernel (two accumulators per pair, one
+    launch; forced here on shapes too small for the automatic choice):
+    against the composition of two plain GEMMs and against the oracle."""
+    _gated_check(m, n, k, dt, {"SP24_NARROW_PAIR": "1"})
 
 
 @pytest.mark.parametrize("outs", ["f32", "bf16", "both"])
