@@ -897,14 +897,17 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   }
 
   if (p.a_c_up != nullptr) {
+    // The gated product, in order of preference (W_gate/W_up 14336 x 4096):
+    //  1. 33..128 columns with enough 256-row tiles: one launch of the
+    //     CTA-pair kernel's gated form (T = 64: 29.1 us, T = 128: 35.1 us);
+    //  2. up to 64 columns, and for wider N while the tile count is modest:
+    //     one launch of the split-K kernel's gated form (T = 16: 26.5 us);
+    //  3. otherwise two passes, each on the kernel the plain dispatch picks
+    //     (65..128 columns with few row tiles: the pair K-split form, which
+    //     beat the one split-K launch, 42.7 us against 46.9 us at T = 128).
+    // SP24_GATED=1|2 forces 2 or 3; SP24_PAIR_GATED (set) skips 1.
     const int bn = std::min(128, choose_bn(d->m, d->n, d->tile_n, di->sm_count));
     const long long tiles = static_cast<long long>((d->m + 127) / 128) * ((d->n + bn - 1) / bn);
-    // Up to 64 columns, and for wider N while the tile count is modest, both
-    // weights stream through one split-K launch.  From 65 columns on, where
-    // the narrow dispatch runs CTA pairs, two pair launches beat it (W_up
-    // shapes, T = 128: 42.7 us against 46.9 us; at T = 64 one launch still
-    // wins, 33.7 us against 36.1 us).  SP24_GATED=1|2 forces one or two
-    // launches.
     int pks = 0;
     const bool pairs_narrow = d->n > 64 && d->n <= 128 &&
                               (narrow_pair_width(d, di->sm_count) > 0 ||
@@ -916,23 +919,23 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     const int npg = narrow_pair_width(d, di->sm_count);
     if (gmode != 1 && gmode != 2 && npg >= 64 && d->n > 32 &&
         std::getenv("SP24_PAIR_GATED") == nullptr) {
-      // One launch on CTA pairs: W_gate and W_up against the same B stages.
+      // 1: W_gate and W_up against the same B stages of a CTA pair.
       LaunchFn pg = d->dtype == SP24_F16    ? pick_pair_gated<0>(npg)
                     : d->dtype == SP24_BF16 ? pick_pair_gated<1>(npg)
                                             : pick_pair_gated<2>(npg);
       return pg(p, *di, stream);
     }
     if (one_launch) {
-      // One launch: both weights through the split-K kernel's ring.
+      // 2: both weights through the split-K kernel's ring.
       LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)
                     : d->dtype == SP24_BF16 ? pick_gated<1>(bn)
                                             : pick_gated<2>(bn);
       return gf(p, *di, stream);
     }
-    // Two passes on the regular kernels with C as the intermediate.  Pass 1
-    // writes act(alpha W_gate B + bias) into C (fp32 when the caller asked
-    // for it, else bf16); pass 2 multiplies (alpha_up W_up B + bias_up) by it
-    // in its epilogue and writes the result.
+    // 3: two passes with C as the intermediate.  Pass 1 writes
+    // act(alpha W_gate B + bias) into C (fp32 when the caller asked for it,
+    // else bf16); pass 2 multiplies (alpha_up W_up B + bias_up) by it in its
+    // epilogue and writes the result.
     Prepared p1 = p;
     p1.a_c_up = nullptr;
     if (p1.c_f32 != nullptr) p1.c_bf16 = nullptr;
