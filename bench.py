@@ -96,6 +96,16 @@ def load_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
+def sustained_dense_peak():
+    """cuBLAS bf16 back to back for seconds under the power cap (or the
+    fallback's 1.4 PF/s): the denominator for runs that the cap holds below
+    the boost clock."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get("bf16_tflops_sustained", 1400.0)
+    return 1400.0
+
+
 def profile_traffic(tag):
     """dram bytes per launch of the bench kernel, from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", f"{tag}.md")
@@ -873,6 +883,8 @@ def main():
                         "peak_basis": f"{peak_src} dense bf16 {dense_peak} TF/s x "
                                       f"{'2 (e4m3) x ' if dt == 2 else ''}16/9 sparse issue ratio",
                         "frac_of_nominal_sparse": kernel_tflops / (4500.0 * peak_scale),
+                        "frac_of_sustained_sparse_peak": kernel_tflops / (
+                            sustained_dense_peak() * peak_scale * SPARSE_OVER_DENSE),
                         "algorithmic_bytes": alg_bytes,
                         "hbm_GBps_at_alg_bytes": alg_bytes / (ms_kernel * 1e-3) / 1e9,
                         "hbm_peak_GBps": hbm_peak}
