@@ -1,9 +1,11 @@
 """The fused all-gather of C over NVLink (sp24_gemm_allgather) on two GPUs.
 
-Each rank computes its 256-aligned column shard of C = A B into its own
-full-width C and, with peer stores, into the other rank's; after a barrier
-both full copies must equal the single-GPU GEMM of the whole problem bit for
-bit (every element is summed in the same K order by whichever kernel runs).
+Each rank computes its column shard of C = A B into its own full-width C and,
+with peer stores, into the other rank's; after a barrier both full copies
+must equal, bit for bit, the same shards computed on one GPU and placed side
+by side (each shard runs the same kernel on either path; whether a shard
+also equals the full-width GEMM depends on the kernel and is tested in
+test_gemm_gpu.py).
 Skipped on a box with fewer than two GPUs.  The ranks are spawned processes
 (NCCL for the barrier, CUDA IPC for the peer buffers); no kernel waits on
 another rank.
@@ -39,13 +41,13 @@ def _worker(rank, world, port, shapes, results):
                             device_id=dev)
     out = []
     try:
-        for (m, n, k, outs) in shapes:
+        for (m, n, k, outs, align) in shapes:
             g = torch.Generator(device=dev).manual_seed(11)
             a = sp24.prune_2of4(torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16))
             b = torch.randn((k, n), device=dev, generator=g).to(torch.bfloat16)
             ac, meta = sp24.compress(a)
             img = sp24.repack_meta(meta, m, k, torch.bfloat16)
-            n0, n1 = sp24.shard_columns(n, world, rank, 256)
+            n0, n1 = sp24.shard_columns(n, world, rank, align)
             full32 = torch.full((m, n), float("nan"), device=dev) if "f32" in outs else None
             full16 = (torch.full((m, n), float("nan"), device=dev, dtype=torch.bfloat16)
                       if "bf16" in outs else None)
@@ -69,8 +71,14 @@ def _worker(rank, world, port, shapes, results):
                 sp24.gemm_allgather(desc, peer_f32=peer32, peer_bf16=peer16)
             torch.cuda.synchronize()
             dist.barrier()
-            ref32, ref16 = sp24.gemm(ac, img, b, m, n, k, meta_format=sp24.META_TC,
-                                     out_bf16=True)
+            ref32 = torch.empty((m, n), device=dev)
+            ref16 = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+            for r in range(world):   # every rank's shard, computed here
+                s0, s1 = sp24.shard_columns(n, world, r, align)
+                if s1 > s0:
+                    sp24.gemm(ac, img, b[:, s0:s1].contiguous(), m, s1 - s0, k,
+                              meta_format=sp24.META_TC, c_f32=ref32[:, s0:s1],
+                              c_bf16=ref16[:, s0:s1])
             torch.cuda.synchronize()
             ok = sp24.last_kernel_status() == 0
             if full32 is not None:
@@ -91,9 +99,12 @@ def test_fused_allgather_two_gpus():
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     world = 2
-    shapes = [(512, 1024, 512, ("f32",)), (256, 768, 1024, ("f32", "bf16")),
-              (1024, 512, 256, ("bf16",)), (384, 4096, 2048, ("f32",)),
-              (128, 512, 2048, ("f32", "bf16"))]   # narrow: split-K kernel, cluster reduce
+    shapes = [(512, 1024, 512, ("f32",), 256), (256, 768, 1024, ("f32", "bf16"), 256),
+              (1024, 512, 256, ("bf16",), 256), (384, 4096, 2048, ("f32",), 256),
+              (128, 512, 2048, ("f32", "bf16"), 256),   # narrow: split-K, cluster reduce
+              # 128 columns per rank: the 128-wide CTA-pair tile (56 row tiles) and
+              # its K-split form (16 row tiles), each with peer stores
+              (14336, 256, 512, ("f32", "bf16"), 128), (4096, 256, 2048, ("f32", "bf16"), 128)]
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     results = mgr.dict()
