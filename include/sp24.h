@@ -185,9 +185,10 @@ sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long ti
 
 /* Allocation-free GEMM (no counterpart in the reference).
    Same contract and results as sp24_gemm, for callers that must not allocate
-   device memory per call: code running inside a stream-capture region or a
-   real-time serving loop that forbids cudaMalloc/cudaFree after start-up, and
-   plugin hosts that hand the library only its inputs and outputs.  Instead of
+   device memory per call: real-time serving loops that forbid
+   cudaMalloc/cudaFree after start-up (an allocation can synchronize the
+   device and stall every stream), and plugin hosts that own all device memory
+   and hand the library only its inputs and outputs.  Instead of
    d->workspace (ignored here) it stages its scratch (the tcgen05 image of
    reference-layout metadata and, when B's row pitch breaks the 16-byte TMA
    rule, a padded copy of B) in one fixed buffer of SP24_NOALLOC_SCRATCH_BYTES

@@ -1,7 +1,8 @@
 """sp24_gemm_noalloc: the allocation-free GEMM entry point for callers that
-may not allocate device memory per call (stream-capture regions, serving
-loops that forbid cudaMalloc after start-up, plugin hosts that only hand over
-inputs and outputs).  It stages its scratch in the library's fixed device
+may not allocate device memory per call (serving loops that forbid
+cudaMalloc after start-up, since an allocation can synchronize the device;
+plugin hosts that own all device memory and only hand over inputs and
+outputs).  It stages its scratch in the library's fixed device
 buffer instead of a caller workspace.
 
 Checked through the C ABI against the regular sp24_gemm (which gets its own
