@@ -1,34 +1,41 @@
-// sp24_gemm2sm_kernel.cuh — the large-problem 2:4 sparse GEMM: a CTA pair
-// (cluster of 2) computes a 256 x 256 tile with tcgen05.mma.sp.cta_group::2.
+// sp24_gemm2sm_kernel.cuh — the 2:4 sparse GEMM on CTA pairs: a cluster of
+// 2 CTAs computes a 256-row tile with tcgen05.mma.sp.cta_group::2.
 //
-// Why a pair: one tcgen05.mma.sp.cta_group::2 with M=256, N=256 reads A_c
-// rows 0-127 and B columns 0-127 from CTA 0's shared memory and A_c rows
-// 128-255 and B columns 128-255 from CTA 1's.  Each SM therefore stages half
-// of B, which (a) halves B's share of the L2->SM traffic and of the shared
-// memory read bandwidth per MMA and (b) lets the same shared-memory ring cover
-// twice the MMA time.  The single-CTA kernel (sp24_gemm_kernel.cuh) was
-// bound by bytes in flight per SM; this one carries 1.6x the FLOPs per staged
-// byte.  No TMA multicast is used: each CTA loads its own tiles.
+// Why a pair: one tcgen05.mma.sp.cta_group::2 with M=256, N=BNP reads A_c
+// rows 0-127 and B columns [0, BNP/2) from CTA 0's shared memory and A_c
+// rows 128-255 and B columns [BNP/2, BNP) from CTA 1's.  Each SM therefore
+// stages half of B, which (a) halves B's share of the L2->SM traffic and of
+// the shared-memory read bandwidth per MMA and (b) lets the same ring cover
+// twice the MMA time.  No TMA multicast is used: each CTA loads its own tiles.
+//
+// Forms (template parameters of pair_gemm_body):
+//   BNP = 256        large problems; the persistent grid walks the tiles.
+//   BNP = 32..128    narrow N (an MLP layer over a few tokens): stages of
+//                    22-36 KB, 6-8 of them in the ring.
+//   G = 2            gated (SwiGLU): W_gate and W_up against the same B
+//                    stages into two accumulators.
+//   KS = 1           K-split: a cluster of 2 S CTAs per tile, pair p summing
+//                    K slice p, partial tiles reduced over distributed shared
+//                    memory (narrow N with few row tiles).
 //
 // Roles per CTA (11 warps):
 //   warps 0,10  TMA producers (both CTAs): warp 0 the A_c rows and the
-//               metadata atom of the CTA's own 128 rows, warp 10 its half of
+//               metadata atoms of the CTA's own 128 rows, warp 10 its half of
 //               the B columns; completion bytes of both CTAs are counted on
-//               the leader's (rank 0) full barrier, which only the leader's
-//               two producer warps arm.
+//               the pair leader's full barrier, which only the leader arms.
 //   warp 1      TMEM owner (alloc/dealloc with cta_group::2 in both CTAs);
-//               in the leader one lane issues tcgen05.cp (metadata of both
-//               CTAs into their own TMEM) and the pair MMAs, and commits with
-//               a 2-CTA multicast so both CTAs' ring slots / accumulator
-//               barriers advance.
+//               in the leader one elected lane issues, per stage, tcgen05.cp
+//               (metadata of both CTAs into their own TMEM), the pair MMAs and
+//               a 2-CTA multicast commit, so both CTAs' ring slots and
+//               accumulator barriers advance.
 //   warps 2-9   epilogue (both CTAs): two warps per TMEM lane quarter, each
-//               pulls 128 accumulator columns of its 32 rows into registers,
+//               pulls BNP/2 accumulator columns of its 32 rows into registers,
 //               hands the accumulator back to the leader's MMA warp at once
 //               (remote mbarrier arrive), then scales / converts / stores
 //               while the next tile's MMAs run.
-// The accumulator (256 columns) plus two metadata buffers (8 columns) fill
-// TMEM, so the accumulator is single-buffered; the register hand-off keeps
-// the MMA pause to the TMEM read time.
+// The accumulator(s) plus two metadata buffers fill TMEM (the 256-wide
+// accumulator alone takes half of it), so the accumulator is single-buffered;
+// the register hand-off keeps the MMA pause to the TMEM read time.
 #pragma once
 
 #include <cuda_bf16.h>
