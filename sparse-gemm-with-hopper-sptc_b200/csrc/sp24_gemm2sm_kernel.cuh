@@ -33,9 +33,9 @@
 //               hands the accumulator back to the leader's MMA warp at once
 //               (remote mbarrier arrive), then scales / converts / stores
 //               while the next tile's MMAs run.
-// The accumulator(s) plus two metadata buffers fill TMEM (the 256-wide
-// accumulator alone takes half of it), so the accumulator is single-buffered;
-// the register hand-off keeps the MMA pause to the TMEM read time.
+// Two 256-wide accumulators plus the two metadata buffers would exceed TMEM's
+// 512 columns, so the accumulator is single-buffered (in every form); the
+// register hand-off keeps the MMA pause to the TMEM read time.
 #pragma once
 
 #include <cuda_bf16.h>
