@@ -30,6 +30,11 @@
 // Roles (6 warps, as in sp24_gemm_kernel.cuh): warp 0 TMA producer, warp 1
 // TMEM owner and MMA issuer, warps 2..5 epilogue (TMEM lane quarters).
 //
+// In the default dispatch this kernel takes up to 16 columns, and wider
+// narrow tiles only where the CTA-pair kernel's narrow forms do not apply
+// (sp24_gemm2sm_kernel.cuh): from 17 columns on, pairs that each stage half
+// of B keep more stages in flight than one SM per 128-row tile.
+//
 // Replaces, for narrow N, the reference's wgmma_sp_raw_kernel<Element,BlockN>
 // (wgmma_sp_raw_common.hpp:955-1030), whose BlockN 8..128 variants compute one
 // 64 x BlockN tile per CTA with one 32/64-wide K step per iteration.
