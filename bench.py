@@ -40,6 +40,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -139,7 +140,10 @@ class ClockSampler:
     def __init__(self, gpus):
         self.gpus = ",".join(str(g) for g in gpus)
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # Raw samples go to a scratch file (SP24_CLOCKS_DIR, else the system's
+        # temporary directory); the JSON line carries their summary.
+        out_dir = os.environ.get("SP24_CLOCKS_DIR", tempfile.gettempdir())
+        self.path = os.path.join(out_dir, f"sp24_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
         try:

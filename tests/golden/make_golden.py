@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a container that has the reference checkout (default /root/reference)
-after ``make -C oracle ref``.  For every reference entry point
+Run where the reference checkout is available (its directory is given with
+--ref-dir) after ``make -C oracle ref``.  For every reference entry point
 ``mma_sp_wgmma_*.cu`` it parses the case table, then replays the suite exactly
 as the reference does (one mt19937 seeded 1234 shared by the cases in table
 order, wgmma_sp_raw_common.hpp:1123-1127) through the reference's own host
@@ -22,7 +22,7 @@ at their own 2048^3 size.
 The CuTe harness (wgmma_sp_demo_common.hpp) shares these host algorithms;
 its suites are recorded the same way.
 
-    python tests/golden/make_golden.py [--ref-dir /root/reference]
+    python tests/golden/make_golden.py [--ref-dir REFERENCE_CHECKOUT]
 """
 from __future__ import annotations
 
