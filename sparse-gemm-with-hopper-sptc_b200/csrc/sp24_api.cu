@@ -631,6 +631,15 @@ bool use_splitk_kernel(int m, int n, int bn, int sm_count) {
   return n <= 128 || tiles <= 4LL * sm_count;
 }
 
+// Split-K tile width for a 16-column choice: 8 for 16-bit types with at most
+// 8 columns, whose 16-column B boxes would be half outside B (the kernel's
+// 8-column form loads in-bounds boxes only).  SP24_SPLITK_B8=0 turns it off.
+int splitk_tile_n(const sp24_gemm_desc* d, int bn) {
+  if (bn != 16 || d->n > 8 || is_fp8(d->dtype)) return bn;
+  const char* env = std::getenv("SP24_SPLITK_B8");
+  return (env != nullptr && std::atoi(env) == 0) ? bn : 8;
+}
+
 // Units per split-K stage: two (32 KB of A_c) for tiles up to 32 wide, one
 // above, where B's share of a stage grows.  SP24_SPLITK_KB=1|2 overrides.
 int splitk_units(int bn) {
@@ -678,6 +687,9 @@ LaunchFn pick_pair(sp24_dtype dt) {
 
 template <int DT>
 LaunchFn pick_splitk(int bn, int kb) {
+  if constexpr (DT != 2) {
+    if (bn == 8) return kb == 2 ? launch_splitk<DT, 8, 2, 1> : launch_splitk<DT, 8, 1, 1>;
+  }
   switch (bn) {
     case 16: return kb == 2 ? launch_splitk<DT, 16, 2, 1> : launch_splitk<DT, 16, 1, 1>;
     case 32: return kb == 2 ? launch_splitk<DT, 32, 2, 1> : launch_splitk<DT, 32, 1, 1>;
@@ -690,6 +702,9 @@ LaunchFn pick_splitk(int bn, int kb) {
 // five slots in flight.
 template <int DT>
 LaunchFn pick_gated(int bn) {
+  if constexpr (DT != 2) {
+    if (bn == 8) return launch_splitk<DT, 8, 1, 2>;
+  }
   switch (bn) {
     case 16: return launch_splitk<DT, 16, 1, 2>;
     case 32: return launch_splitk<DT, 32, 1, 2>;
@@ -927,9 +942,10 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     }
     if (one_launch) {
       // 2: both weights through the split-K kernel's ring.
-      LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(bn)
-                    : d->dtype == SP24_BF16 ? pick_gated<1>(bn)
-                                            : pick_gated<2>(bn);
+      const int sbn = splitk_tile_n(d, bn);
+      LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(sbn)
+                    : d->dtype == SP24_BF16 ? pick_gated<1>(sbn)
+                                            : pick_gated<2>(sbn);
       return gf(p, *di, stream);
     }
     // 3: two passes with C as the intermediate.  Pass 1 writes
@@ -979,9 +995,10 @@ sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const Devic
   }
   if (use_splitk_kernel(d->m, d->n, bn, di->sm_count)) {
     const int kb = splitk_units(bn);
-    LaunchFn sf = d->dtype == SP24_F16    ? pick_splitk<0>(bn, kb)
-                  : d->dtype == SP24_BF16 ? pick_splitk<1>(bn, kb)
-                                          : pick_splitk<2>(bn, kb);
+    const int sbn = splitk_tile_n(d, bn);
+    LaunchFn sf = d->dtype == SP24_F16    ? pick_splitk<0>(sbn, kb)
+                  : d->dtype == SP24_BF16 ? pick_splitk<1>(sbn, kb)
+                                          : pick_splitk<2>(sbn, kb);
     return sf(p, *di, stream);
   }
   LaunchFn fn = d->dtype == SP24_F16    ? pick_bn<0>(bn)

@@ -83,9 +83,17 @@ struct SplitParams {
 };
 
 // G: weights streamed per CTA (1 plain, 2 gated).
+// BN = 8 (16-bit types, N <= 8): 8-column tiles on N = 16 MMAs.  A 16-wide
+// box over an 8-column B would be half outside the tensor, and TMA's
+// zero-fill of those halves slowed the whole launch (W_up 14336 x 4096, 8
+// columns: 16.8 us against 14.8 us at 16 columns).  Instead each unit loads
+// one in-bounds 8-column box (16 B rows, no swizzle), and the MMA's second
+// 8-column chunk reads a region that the kernel zeroes once, so accumulator
+// columns 8..15 stay zero and are never stored.
 template <int DT, int BN, int KB, int G = 1>
 struct SplitCfg {
   static constexpr int ESZ = (DT == 2) ? 1 : 2;
+  static constexpr int MMA_N = BN < 16 ? 16 : BN;         // accumulator columns per weight
   static constexpr int KIND = (DT == 2) ? 1 : 0;
   static constexpr int WEIGHTS = G;
   static constexpr int UK = (DT == 2) ? 256 : 128;        // dense K per unit
@@ -99,10 +107,12 @@ struct SplitCfg {
   static constexpr int B_ROW = BN * ESZ;
   static constexpr int B_SPAN = B_ROW >= 128 ? 128 : B_ROW;
   static constexpr int B_BOXN = B_SPAN / ESZ;
-  static constexpr int B_BOXES = BN / B_BOXN;             // per unit
+  static constexpr int B_BOXES = BN / B_BOXN;             // loaded per unit
+  static constexpr int B_CHUNKS = MMA_N / B_BOXN;         // read per unit by the MMAs
   static constexpr int B_BOX_BYTES = B_SPAN * UK;
-  static constexpr int B_UNIT = B_BOX_BYTES * B_BOXES;
+  static constexpr int B_UNIT = B_BOX_BYTES * B_CHUNKS;   // chunks past B_BOXES: zeroes
   static constexpr int B_BYTES = KB * B_UNIT;
+  static constexpr int B_LOAD_BYTES = KB * B_BOXES * B_BOX_BYTES;
   static constexpr uint32_t B_LAYOUT =
       B_SPAN == 128 ? kLayoutSW128 : B_SPAN == 64 ? kLayoutSW64 : B_SPAN == 32 ? kLayoutSW32
                                                                              : kLayoutNone;
@@ -119,7 +129,7 @@ struct SplitCfg {
   static constexpr int LOADS_B = KB * B_BOXES;
   static constexpr int LOADS = LOADS_A + LOADS_B + G * E_S;   // one copy per producer lane
   static constexpr uint32_t LOAD_LANES = LOADS == 32 ? 0xffffffffu : (1u << LOADS) - 1u;
-  static constexpr int E_COL = G * BN;                    // accumulators first, then metadata
+  static constexpr int E_COL = G * MMA_N;                 // accumulators first, then metadata
   static constexpr int COLS_NEEDED = E_COL + 2 * G * E_S * 4;
   static constexpr uint32_t TMEM_COLS = COLS_NEEDED <= 32    ? 32
                                         : COLS_NEEDED <= 64  ? 64
@@ -127,11 +137,13 @@ struct SplitCfg {
                                         : COLS_NEEDED <= 256 ? 256
                                                              : 512;
   static constexpr uint32_t FMT = (DT == 1) ? 1u : 0u;
-  static constexpr uint32_t IDESC = make_idesc_sparse(FMT, BN, kBlockM, true);
-  static constexpr int CH = BN < 32 ? BN : 32;
+  static constexpr uint32_t IDESC = make_idesc_sparse(FMT, MMA_N, kBlockM, true);
+  static constexpr int CH = MMA_N < 32 ? MMA_N : 32;      // accumulator columns per TMEM load
+  static constexpr int CW = CH < BN ? CH : BN;            // ... of which output columns
   static constexpr int RS = BN + 4;                       // partial-tile row stride (floats)
 
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 128, "narrow tiles: N % 16 == 0, 16..128");
+  static_assert((BN % 16 == 0 && BN >= 16 && BN <= 128) || (BN == 8 && ESZ == 2),
+                "narrow tiles: N % 16 == 0, 16..128, or 8 for 16-bit types");
   static_assert(BN % B_BOXN == 0, "B tile must be whole TMA boxes");
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(STAGE_BYTES % 1024 == 0, "stage regions must stay 1024-aligned");
@@ -147,7 +159,7 @@ SP24_DEV uint32_t split_stage_tx(const SplitParams& P, int g) {
   const int a0 = g * C::E_S;
   int atoms = P.katoms - a0;
   atoms = atoms < 0 ? 0 : (atoms > C::E_S ? C::E_S : atoms);
-  return static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + C::WEIGHTS * atoms * kAtomBytes);
+  return static_cast<uint32_t>(C::A_BYTES + C::B_LOAD_BYTES + C::WEIGHTS * atoms * kAtomBytes);
 }
 
 // Stores four finished values of one row into one copy of C.
@@ -272,6 +284,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
     tmem_relinquish();
+  }
+  if constexpr (C::B_CHUNKS > C::B_BOXES) {
+    // BN = 8: the B chunks that no TMA copy writes hold zeroes for the whole
+    // launch, in every unit of every ring slot.
+    constexpr int ZV = (C::B_CHUNKS - C::B_BOXES) * C::B_BOX_BYTES / 16;   // stores per unit
+    for (int i = threadIdx.x; i < C::STAGES * KB * ZV; i += kThreads) {
+      const int slot = i / (KB * ZV);
+      const int u = (i / ZV) % KB;
+      const int v = i % ZV;
+      *reinterpret_cast<uint4*>(smem + slot * C::STAGE_BYTES + C::A_BYTES + u * C::B_UNIT +
+                                C::B_BOXES * C::B_BOX_BYTES + v * 16) = make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();   // visible to the MMAs (async proxy) after the barrier
   }
   tc_fence_before();
   __syncthreads();
@@ -398,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t col = (C::KIND == 0) ? static_cast<uint32_t>((kk % 128) / 32)
                                                     : static_cast<uint32_t>(2 * ((kk % 128) / 64));
                 tc_mma<1, C::KIND>(
-                    tmem_base + static_cast<uint32_t>(w * BN),
+                    tmem_base + static_cast<uint32_t>(w * C::MMA_N),
                     adesc0 + soff + (w * KB + u) * (C::A_BOX >> 4) + j * 2,
                     bdesc0 + soff + u * (C::B_UNIT >> 4) + j * (C::B_MMA_ADVANCE >> 4),
                     e_tmem + 4 * atom_in + (col & ~1u), C::IDESC | P.idesc_ab | (col & 1u),
@@ -442,9 +467,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int w = 0; w < G; ++w) {
           if constexpr (C::CH == 32) {
-            tmem_ld_x32(tb + static_cast<uint32_t>(w * BN + c), r[w]);
+            tmem_ld_x32(tb + static_cast<uint32_t>(w * C::MMA_N + c), r[w]);
           } else {
-            tmem_ld_x16(tb + static_cast<uint32_t>(w * BN + c), r[w]);
+            tmem_ld_x16(tb + static_cast<uint32_t>(w * C::MMA_N + c), r[w]);
           }
         }
 #pragma unroll
@@ -452,21 +477,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (S == 1) {
           // Finished values of this lane's row go to the warp's rows of the
           // idle ring; the warp then stores them row by row (below).
-          float v[C::CH];
+          float v[C::CW];
 #pragma unroll
-          for (int e = 0; e < C::CH; ++e)
+          for (int e = 0; e < C::CW; ++e)
             v[e] = split_out<G>(P, __uint_as_float(r[0][e]), __uint_as_float(r[G - 1][e]), bg,
                                 bu);
-          if (P.gate_from_c && live) gate_mul_row<C::CH>(P, v, row, nb * BN + c);
+          if (P.gate_from_c && live) gate_mul_row<C::CW>(P, v, row, nb * BN + c);
 #pragma unroll
-          for (int e = 0; e < C::CH; e += 4)
+          for (int e = 0; e < C::CW; e += 4)
             *reinterpret_cast<float4*>(red + row_l * C::RS + c + e) =
                 make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
         } else {
 #pragma unroll
           for (int w = 0; w < G; ++w)
 #pragma unroll
-            for (int v = 0; v < C::CH; v += 4)
+            for (int v = 0; v < C::CW; v += 4)
               *reinterpret_cast<float4*>(red + (w * kBlockM + row_l) * C::RS + c + v) =
                   make_float4(__uint_as_float(r[w][v]), __uint_as_float(r[w][v + 1]),
                               __uint_as_float(r[w][v + 2]), __uint_as_float(r[w][v + 3]));

@@ -38,6 +38,12 @@ SP24_DEV void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Orders this thread's ordinary shared-memory stores before later reads of
+// the same bytes by the async proxy (tcgen05.mma operands, TMA).
+SP24_DEV void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 SP24_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
                    smem_u32(bar)),

@@ -419,6 +419,58 @@ def test_splitk_matches_oracle(dt, m, n, k, splits, kb):
     assert (c - c_one).abs().max().item() <= 1e-5 * scale
 
 
+EIGHT_COLUMN_CASES = [
+    # m, n, k, K slices ("" = the dispatch's choice)
+    (256, 8, 4096, ""),
+    (200, 5, 2112, "3"),      # ragged M, N and last stage; B staged at a 16 B pitch
+    (4096, 8, 2048, "4"),
+    (14336, 8, 4096, ""),     # W_up at T = 8
+    (130, 1, 256, "1"),
+]
+
+
+@pytest.mark.parametrize("dt", [0, 1])
+@pytest.mark.parametrize("m,n,k,splits", EIGHT_COLUMN_CASES)
+def test_splitk_eight_column_form(dt, m, n, k, splits):
+    """16-bit B with at most 8 columns: the split-K kernel's 8-column form
+    (one in-bounds 8-column B box per unit; N = 16 MMAs whose second chunk
+    reads zeroes) against its 16-column form (SP24_SPLITK_B8=0), which sums
+    the same products in the same order: bit-identical fp32 and bf16 outputs
+    for the plain GEMM, the bias + SiLU epilogue and the gated form.  Also
+    within the row-norm bound of the oracle on up to 64 sampled rows."""
+    g = torch.Generator(device=DEV).manual_seed(m + n + k + dt)
+    tdt = torch.float16 if dt == 0 else torch.bfloat16
+    a = sp24.prune_2of4(torch.randn((m, k), device=DEV, generator=g).to(tdt))
+    a_up = sp24.prune_2of4(torch.randn((m, k), device=DEV, generator=g).to(tdt))
+    b = torch.randn((k, n), device=DEV, generator=g).to(tdt)
+    bias = torch.randn((m,), device=DEV, generator=g)
+    ac, e = sp24.compress(a)
+    acu, eu = sp24.compress(a_up)
+    img, img_u = sp24.repack_meta(e, m, k, tdt), sp24.repack_meta(eu, m, k, tdt)
+    env = {"SP24_SPLITS": splits} if splits else {}
+
+    def run():
+        plain = sp24.gemm(ac, e, b, m, n, k, out_bf16=True, dtype=tdt)
+        silu = sp24.gemm_fused(ac, img, b, m, n, k, bias=bias, act=sp24.ACT_SILU, dtype=tdt)
+        gated = sp24.gemm_fused(ac, img, b, m, n, k, act=sp24.ACT_SILU, a_c_up=acu,
+                                meta_up=img_u, alpha_up=0.5, out_bf16=True, dtype=tdt)
+        return [t for pair in (plain, silu, gated) for t in pair if t is not None]
+
+    got = _with_env(env, run)
+    want = _with_env({**env, "SP24_SPLITK_B8": "0"}, run)
+    torch.cuda.synchronize()
+    assert sp24.last_kernel_status() == 0
+    for x, y in zip(got, want):
+        assert torch.equal(x, y)
+    rows = np.arange(m) if m <= 256 else np.sort(
+        np.random.default_rng(m).choice(m, 64, replace=False))
+    a_bits, b_bits = to_host_bits(a)[rows], to_host_bits(b)
+    ref = oracle.gemm(dt, a_bits, b_bits, threads=8)
+    err = oracle.row_norm_rel_error(got[0][rows].cpu().numpy(), ref, oracle.to_float(dt, a_bits),
+                                    oracle.to_float(dt, b_bits))
+    assert err <= TOL[dt], err
+
+
 def test_splitk_mlp_shapes_default_dispatch():
     """Configuration 4's narrow shapes through the default dispatch (W_down:
     M = 4096, K = 14336, T = 8 splits K; W_up: M = 14336, T = 16 does not),
