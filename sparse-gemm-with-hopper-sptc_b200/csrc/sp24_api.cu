@@ -317,6 +317,14 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
                : (aligned32(p.c_bf16) && (p.ldc % 16) == 0) ? 2
                : (aligned16(p.c_bf16) && (p.ldc % 8) == 0)  ? 1
                                                             : 0;
+  // C under an L2 evict-first policy, so the output does not push the A and B
+  // tiles that other CTAs still read out of L2 (configuration 2, fp32 + bf16
+  // out: +1%).  The fused all-gather and the second gated pass read C back
+  // and keep the default policy.  SP24_C_EVICT=0 turns it off.
+  const char* cev = std::getenv("SP24_C_EVICT");
+  P.c_evict_first = ((cev == nullptr || std::atoi(cev) != 0) && p.peers.n == 0 && !p.gate_from_c)
+                        ? 1
+                        : 0;
   P.status = p.status;
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;

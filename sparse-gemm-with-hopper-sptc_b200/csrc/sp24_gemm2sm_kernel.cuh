@@ -71,6 +71,7 @@ struct PairParams {
                       // already in C (c_f32 if given, else c_bf16) before storing
   int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
   int vec_bf16;
+  int c_evict_first;  // 32-byte C stores under an L2 evict-first policy (no peers)
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -230,6 +231,7 @@ template <int CW>
 SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
                                 const uint32_t (&r)[CW], int row, int col0) {
   const bool full = col0 + CW <= P.n;
+  const uint64_t pol = P.c_evict_first ? l2_evict_first_policy() : 0;
   if (c32 != nullptr) {
     float* dst = c32 + static_cast<long long>(row) * P.ldc + col0;
     if (full && P.vec_f32 == 2) {
@@ -238,7 +240,10 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]);
-        st_global_v8(dst + i, v);
+        if (P.c_evict_first)
+          st_global_v8_hint(dst + i, v, pol);
+        else
+          st_global_v8(dst + i, v);
       }
     } else if (full && P.vec_f32 == 1) {
 #pragma unroll
@@ -265,7 +270,10 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
           pk[j] = *reinterpret_cast<uint32_t*>(&h);
         }
         if (P.vec_bf16 == 2) {
-          st_global_v8_u32(dst + i, pk);
+          if (P.c_evict_first)
+            st_global_v8_u32_hint(dst + i, pk, pol);
+          else
+            st_global_v8_u32(dst + i, pk);
         } else {
           *reinterpret_cast<uint4*>(dst + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(dst + i + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);

@@ -419,6 +419,30 @@ SP24_DEV void st_global_v8(float* p, const float* v) {
                : "memory");
 }
 
+// L2 cache policy that marks the lines it touches first for eviction: for
+// output that nothing in the kernel reads again, so it does not push the
+// reused operand tiles out of L2.
+SP24_DEV uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 32-byte global stores under an L2 cache policy.
+SP24_DEV void st_global_v8_hint(float* p, const float* v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8}, %9;" ::"l"(p),
+               "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]),
+               "f"(v[7]), "l"(pol)
+               : "memory");
+}
+
+SP24_DEV void st_global_v8_u32_hint(void* p, const uint32_t* v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8}, %9;" ::"l"(p),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+               "r"(v[7]), "l"(pol)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 format):
 //   [0,14) start address >> 4, [16,30) leading byte offset >> 4,
