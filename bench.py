@@ -22,10 +22,11 @@ decode pass do (--l2 clean instead cleans L2 before every step and times each
 step alone).
 
 Metric: dense-equivalent TFLOP/s (2MNK/t).  `roofline` compares the kernel
-with the sparse tensor peak derived from the measured dense bf16 peak
-(MEASURED_PEAKS.json) times the hardware's sparse/dense issue ratio 16/9
-(ncu: sm__ops_path_tensor_op_hmma_src_bf16_dst_fp32_sparsity_{on,off}
-.peak_sustained = 3640.9 / 2048 per cycle).  `e2e` runs the same GEMM end
+with the sparse tensor peak: the larger of twice the measured dense peak
+(MEASURED_PEAKS.json, cuBLAS bf16; twice that again for fp8) and the rate
+the tensor pipe itself reaches on this GPU, measured in the same run by the
+probe in lib/libsp24_peak.so (the CTA-pair kernel's own tcgen05.mma.sp shape
+issued back to back from operands resident in shared memory).  `e2e` runs the same GEMM end
 to end through sp24_gemm with host buffers: pinned H2D of A_c + reference
 metadata + B, the GEMM (metadata repack included), D2H of C.
 `cpu_baseline` / `--impl reference` time the reference's own CPU path
@@ -49,7 +50,6 @@ sys.path.insert(0, PKG)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 METRIC = "2:4 GEMM dense-equiv TFLOP/s & % of sparse tensor peak at 1/2/4/8 B200"
-SPARSE_OVER_DENSE = 3640.888889 / 2048.0      # bf16/fp16 sparse vs dense issue rate
 PAIRS = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
 
 CONFIGS = {
@@ -105,6 +105,36 @@ def sustained_dense_peak():
     if os.path.exists(p):
         return json.load(open(p)).get("bf16_tflops_sustained", 1400.0)
     return 1400.0
+
+
+def probe_peaks(dt):
+    """The tensor pipe's own ceiling for dtype dt (0 f16, 1 bf16, 2 e4m3), in
+    dense-equivalent TF/s: the CTA-pair MMA shape issued back to back from
+    shared-memory-resident operands on every SM (lib/libsp24_peak.so), sparse
+    and dense, each the best of three short bursts.  None when the probe is
+    not built."""
+    import sp24
+    try:
+        sp = max(sp24.probe_mma_rate(dt, True, iters=8192, reps=3)[0] for _ in range(3))
+        dn = max(sp24.probe_mma_rate(dt, False, iters=8192, reps=3)[0] for _ in range(3))
+    except (FileNotFoundError, OSError):
+        return None
+    return {"sparse_tflops": sp, "dense_tflops": dn, "sparse_over_dense": sp / dn,
+            "how": "lib/libsp24_peak.so: tcgen05.mma(.sp).cta_group::2 M=256 N=256 from resident "
+                   "shared-memory operands, all SMs, best of 3 bursts of ~2.5 ms"}
+
+
+def sparse_peak(dt, dense_peak, probe):
+    """Roofline denominator: max(2 x measured dense, measured sparse), where
+    the measured dense figure is cuBLAS bf16 from MEASURED_PEAKS.json (doubled
+    for fp8, which MEASURED_PEAKS does not measure) and the measured sparse
+    one is the probe's."""
+    two_dense = 2.0 * dense_peak * (2.0 if dt == 2 else 1.0)
+    if probe is None:
+        return two_dense, "2 x measured dense (no probe)"
+    if probe["sparse_tflops"] >= two_dense:
+        return probe["sparse_tflops"], "probe sparse rate (above 2 x measured dense)"
+    return two_dense, "2 x measured dense (above the probe's sparse rate)"
 
 
 def profile_traffic(tag):
@@ -292,28 +322,58 @@ def cpu_reference_rate(cfg, seconds=10.0, threads=None):
         f"{t:.1f} s")
 
 
+def reference_inputs(cfg, torch):
+    """The workload's 2:4 A and dense B (16-bit types) for the reference arm,
+    with no sp24 code on the way: A and B are drawn on the device as
+    make_inputs draws them, and A is compressed on the host by the
+    reference's own compress_structured_sparse_a (oracle/_ref, compiled from
+    the reference sources).  Returns device (A_c, metadata bytes, B)."""
+    import numpy as np
+    import oracle
+    dev = torch.device("cuda")
+    dt, m, n, k = cfg["dt"], cfg["m"], cfg["n"], cfg["k"]
+    tdt = torch.float16 if dt == 0 else torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1234)
+    gb = torch.Generator(device=dev).manual_seed(4321)
+    pat = torch.randint(0, 6, (m, k // 4), device=dev, generator=g)
+    if cfg["dist"] == "uniform":
+        vals = torch.rand((m, k // 4, 2), device=dev, generator=g) * 2 - 1
+        b = torch.rand((k, n), device=dev, generator=gb) * 2 - 1
+    else:
+        vals = torch.randn((m, k // 4, 2), device=dev, generator=g)
+        b = torch.randn((k, n), device=dev, generator=gb)
+    vals = torch.where(vals.abs() < 1e-3, torch.full_like(vals, 0.5), vals)
+    a = torch.zeros((m, k // 4, 4), device=dev)
+    a.scatter_(2, torch.tensor(PAIRS, device=dev)[pat], vals)
+    a_bits = a.reshape(m, k).to(tdt).cpu().view(torch.int16).numpy().view(np.uint16)
+    del a, vals, pat
+    ac = np.empty((m, k // 2), np.uint16)
+    meta = np.empty((m, k // 8), np.uint8)
+    oracle.ref_lib().ref_compress(dt, a_bits.ctypes.data, m, k, ac.ctypes.data, meta.ctypes.data)
+    ac_t = torch.from_numpy(ac.view(np.int16)).view(tdt).to(dev)
+    return ac_t, torch.from_numpy(meta).to(dev), b.to(tdt)
+
+
 def reference_gpu_legacy(args, cfg):
     """The reference's only kernels that run on sm_100: its legacy warp-level
     mma.sp.sync GEMMs (mma_sp_m16n8k32_fp32{fp16,bf16}.cu, built for sm_100a
     from the reference sources by oracle/Makefile), timed on this GPU over the
-    same workload with CUDA events.  Inputs are made on the device (sp24's
-    compression, bit-exact with the reference's; the k32 kernels read the
-    reference's row-major metadata bytes as words); the timed launches are the
-    reference's kernel alone, fp32 output only.  None when the config has no
-    such kernel (e4m3) or its shape does not tile by 64."""
+    same workload with CUDA events.  Inputs come from reference_inputs (the
+    reference's own host compression; the k32 kernels read its row-major
+    metadata bytes as words); the timed launches are the reference's kernel
+    alone, fp32 output only.  None when the config has no such kernel (e4m3)
+    or its shape does not tile by 64."""
     import oracle
-    if cfg["dt"] not in (0, 1) or not oracle.ref_legacy_available():
+    if cfg["dt"] not in (0, 1) or not oracle.ref_legacy_available() or not oracle.ref_available():
         return None
     m, n, k = cfg["m"], cfg["n"], cfg["k"]
     if m % 64 or n % 64 or k % 32:
         return None
     import torch
-    import sp24
     if not torch.cuda.is_available():
         return None
     which = 2 if cfg["dt"] == 0 else 3
-    ac, meta, img, b, _ = make_inputs(cfg, 0, torch, sp24)
-    del img
+    ac, meta, b = reference_inputs(cfg, torch)
     c = torch.empty((m, n), device=ac.device)
     stream = torch.cuda.current_stream()
 
@@ -395,6 +455,8 @@ def main():
                          "shards + column permute; fused = sp24_gemm_allgather (peer stores "
                          "over NVLink inside the GEMM)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-probe", action="store_true",
+                    help="skip the tensor-pipe probe (roofline peak = 2 x measured dense)")
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--tokens", type=int, default=4096,
                     help="configuration 4: activation columns T (8, 16, 64, 128 or 4096)")
@@ -865,8 +927,8 @@ def main():
 
     if rank == 0:
         dense_peak, hbm_peak, peak_src = load_peaks()
-        peak_scale = 2.0 if dt == 2 else 1.0       # e4m3 issues at twice the 16-bit rate
-        sparse_peak = dense_peak * peak_scale * SPARSE_OVER_DENSE
+        probe = probe_peaks(dt) if not args.no_probe else None
+        peak, peak_why = sparse_peak(dt, dense_peak, probe)
         alg_bytes = in_bytes + out_bytes
         ms_kernel = ms_local / args.steps
         hbm_bound = args.config == 4 and n <= 128
@@ -879,16 +941,18 @@ def main():
                         "frac": gbps / hbm_peak, "traffic": profile_traffic(tag),
                         "peak_basis": f"{peak_src} HBM copy bandwidth",
                         "algorithmic_bytes": alg_bytes, "tflops": kernel_tflops,
-                        "frac_of_sparse_tensor_peak": kernel_tflops / sparse_peak}
+                        "frac_of_sparse_tensor_peak": kernel_tflops / peak}
         else:
-            roofline = {"bound": "tensor", "achieved": kernel_tflops, "peak": sparse_peak,
-                        "unit": "TFLOP/s", "frac": kernel_tflops / sparse_peak,
+            scale = 2.0 if dt == 2 else 1.0
+            roofline = {"bound": "tensor", "achieved": kernel_tflops, "peak": peak,
+                        "unit": "TFLOP/s", "frac": kernel_tflops / peak,
                         "traffic": profile_traffic(tag),
-                        "peak_basis": f"{peak_src} dense bf16 {dense_peak} TF/s x "
-                                      f"{'2 (e4m3) x ' if dt == 2 else ''}16/9 sparse issue ratio",
-                        "frac_of_nominal_sparse": kernel_tflops / (4500.0 * peak_scale),
-                        "frac_of_sustained_sparse_peak": kernel_tflops / (
-                            sustained_dense_peak() * peak_scale * SPARSE_OVER_DENSE),
+                        "peak_basis": f"{peak_why}; measured dense = {peak_src} cuBLAS bf16 "
+                                      f"{dense_peak} TF/s" + (" x 2 for fp8" if dt == 2 else ""),
+                        "probe": probe,
+                        "frac_of_nominal_sparse": kernel_tflops / (4500.0 * scale),
+                        "frac_of_2x_sustained_dense": kernel_tflops / (
+                            2.0 * sustained_dense_peak() * scale),
                         "algorithmic_bytes": alg_bytes,
                         "hbm_GBps_at_alg_bytes": alg_bytes / (ms_kernel * 1e-3) / 1e9,
                         "hbm_peak_GBps": hbm_peak}
@@ -910,7 +974,7 @@ def main():
                               + (", SP24_HINT_STATIC_WEIGHTS" if static_hint else "")
                               if copies > 1 else
                               "no flush: inputs + outputs exceed twice the 126 MB L2")},
-            "pct_of_sparse_peak": 100.0 * kernel_tflops / sparse_peak,
+            "pct_of_sparse_peak": 100.0 * kernel_tflops / peak,
             "roofline": roofline,
             "clocks": clk.summary(),
             "gpu_launches": args.steps,

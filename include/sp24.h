@@ -175,6 +175,13 @@ sp24_status sp24_last_kernel_status(sp24_stream_t stream);
 void sp24_set_launch_hints(unsigned hints);
 unsigned sp24_get_launch_hints(void);
 
+/* Re-reads the SP24_* tuning variables of the environment (no reference
+   counterpart).  The library reads them once, on the first GEMM call, so
+   that a launch scans no environment; they only force a kernel family or a
+   tile parameter for tests and tuning runs.  A caller that changes them
+   afterwards calls this, with no GEMM call in progress on another thread. */
+void sp24_reload_tuning(void);
+
 /* Self-test of the bounded-wait path (no reference counterpart): launches the
    GEMM of `d` with a producer that issues no load, so the consumers' waits run
    out after `timeout_ns`; the kernel frees its TMEM and returns.  Requires

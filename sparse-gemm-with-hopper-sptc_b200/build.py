@@ -10,6 +10,9 @@
                    include searches the including file's directory first, so
                    each main is reached through a symlink in _build/dropin/
                    that sits next to the drop-in headers.
+  build_probe()    lib/libsp24_peak.so — the tensor-core rate probe that bench.py
+                   and the tests use to measure the roofline's peak (measurement
+                   infrastructure, not part of the C ABI).
   build_oracle()   oracle/lib + oracle/_ref (test infrastructure, see oracle/).
 
 ``python sparse-gemm-with-hopper-sptc_b200/build.py [--force]`` builds all.
@@ -58,9 +61,23 @@ def build_lib(force: bool = False) -> str:
     return out
 
 
+def build_probe(force: bool = False) -> str:
+    os.makedirs(LIBDIR, exist_ok=True)
+    out = os.path.join(LIBDIR, "libsp24_peak.so")
+    deps = [os.path.join(CSRC, f) for f in LIB_DEPS + ["sp24_peak.cu"]]
+    if force or _stale(out, deps):
+        tmp = out + ".tmp"
+        _run([NVCC, *ARCH, *COMMON, "-shared", "-o", tmp, os.path.join(CSRC, "sp24_peak.cu")])
+        os.replace(tmp, out)
+    return out
+
+
 DROPIN = os.path.join(HERE, "dropin")
 BINDIR = os.path.join(HERE, "bin")
-REF_DIR = os.environ.get("SP24_REF_DIR", "/root/reference")
+# The reference checkout: SP24_REF_DIR, else a `reference` directory beside
+# the repository.  Only the drop-in and oracle builds read it, and only when
+# it exists.
+REF_DIR = os.environ.get("SP24_REF_DIR", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def dropin_mains(ref_dir: str = REF_DIR):
@@ -83,11 +100,16 @@ def build_dropin(ref_dir: str = REF_DIR, force: bool = False):
     stage = os.path.join(HERE, "_build", "dropin")
     os.makedirs(stage, exist_ok=True)
     os.makedirs(BINDIR, exist_ok=True)
-    for h in ("wgmma_sp_raw_common.hpp", "wgmma_sp_demo_common.hpp", "sp24_host_utils.hpp"):
+    for h in ("wgmma_sp_raw_common.hpp", "wgmma_sp_demo_common.hpp", "sp24_host_utils.hpp",
+              "sp24_raw_kernel.cuh"):
         link = os.path.join(stage, h)
         if not os.path.islink(link):
             os.symlink(os.path.join(DROPIN, h), link)
-    deps = [lib, os.path.join(ROOT, "include", "sp24.h")] + [
+    # sp24_raw_kernel.cuh includes ../csrc/sp24_ptx.cuh relative to the stage
+    csrc_link = os.path.join(HERE, "_build", "csrc")
+    if not os.path.islink(csrc_link):
+        os.symlink(CSRC, csrc_link)
+    deps = [lib, os.path.join(ROOT, "include", "sp24.h"), os.path.join(CSRC, "sp24_ptx.cuh")] + [
         os.path.join(DROPIN, h) for h in os.listdir(DROPIN)]
     built = []
     for path in mains:
@@ -105,6 +127,27 @@ def build_dropin(ref_dir: str = REF_DIR, force: bool = False):
     return built
 
 
+def build_raw_kernel_check(force: bool = False):
+    """bin/raw_kernel_check (M = 64 form, the default) and
+    bin/raw_kernel_check_m128 (M = 128 form): tests/raw_kernel_check.cu, the
+    launchable wgmma_sp_raw_kernel run over the reference entry points'
+    cases.  Test infrastructure."""
+    lib = build_lib()
+    os.makedirs(BINDIR, exist_ok=True)
+    src = os.path.join(ROOT, "tests", "raw_kernel_check.cu")
+    deps = [lib, src, os.path.join(CSRC, "sp24_ptx.cuh"), os.path.join(ROOT, "include", "sp24.h")] + [
+        os.path.join(DROPIN, h) for h in os.listdir(DROPIN)]
+    outs = []
+    for name, layout in (("raw_kernel_check", 1), ("raw_kernel_check_m128", 0)):
+        out = os.path.join(BINDIR, name)
+        if force or _stale(out, deps):
+            _run([NVCC, *ARCH, "-O2", "-std=c++17", f"-DSP24_RAW_LAYOUT={layout}",
+                  "-I" + os.path.join(ROOT, "include"), "-I" + DROPIN, src,
+                  "-L" + LIBDIR, "-lsp24", "-Xlinker", "-rpath,$ORIGIN/../lib", "-o", out])
+        outs.append(out)
+    return outs
+
+
 def build_oracle(ref_dir: str = REF_DIR) -> None:
     """CPU oracle (always) and the reference harness (when the checkout exists)."""
     oracle_dir = os.path.join(ROOT, "oracle")
@@ -116,8 +159,10 @@ def build_oracle(ref_dir: str = REF_DIR) -> None:
 
 def build_all(force: bool = False) -> None:
     build_lib(force=force)
+    build_probe(force=force)
     build_oracle()
     build_dropin(force=force)
+    build_raw_kernel_check(force=force)
 
 
 if __name__ == "__main__":

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -154,6 +155,96 @@ CUtensorMapSwizzle swizzle_for_span(int span) {
 // Launch hints of the calling host thread (sp24_set_launch_hints).
 thread_local unsigned g_launch_hints = SP24_HINT_NONE;
 
+// Tuning switches from the environment.  None is needed in normal use: they
+// force a kernel family or a tile parameter for tests and tuning runs.  They
+// are read once, on the first call that needs them, so a launch costs no
+// getenv scan; sp24_reload_tuning() reads them again after the caller changed
+// the environment.  Every launch works on its own copy, taken under a mutex.
+struct Tuning {
+  int pdl = 1;                // SP24_PDL=0: no programmatic dependent launch
+  int group_m = 0;            // SP24_GROUP_M: CTA-pair tile rasterisation group (0 = default)
+  int c_evict = 1;            // SP24_C_EVICT=0: C stores without the evict-first policy
+  int splits = 0;             // SP24_SPLITS: split-K slices (0 = chosen per shape)
+  int krot = 1;               // SP24_KROT=0: split-K tiles all start at K = 0
+  int pair_fine = 0;          // SP24_PAIR_FINE=1: half-size CTA-pair stages
+  int kernel_set = 0;         // SP24_KERNEL is set (a forced kernel family wins)
+  int kernel = 0;             //   0 other, 1 "1sm", 2 "2sm", 3 "splitk"
+  int narrow_pair = -1;       // SP24_NARROW_PAIR=0|1 (-1 unset)
+  int pair_splitk = -1;       // SP24_PAIR_SPLITK=0|S (-1 unset)
+  int pair_splitk_width = 0;  // SP24_PAIR_SPLITK_WIDTH=64|128 (0 unset)
+  int splitk_b8 = 1;          // SP24_SPLITK_B8=0: no 8-column split-K form
+  int splitk_kb = 0;          // SP24_SPLITK_KB=1|2 (0 = chosen per tile width)
+  int gated = 0;              // SP24_GATED=1|2: gated SwiGLU form forced
+  int pair_gated = 1;         // SP24_PAIR_GATED set: gated CTA-pair form off
+};
+
+Tuning read_tuning() {
+  Tuning t;
+  auto num = [](const char* name, int* out) {
+    const char* v = std::getenv(name);
+    if (v == nullptr) return false;
+    *out = std::atoi(v);
+    return true;
+  };
+  int v = 0;
+  if (num("SP24_PDL", &v)) t.pdl = v != 0;
+  if (num("SP24_GROUP_M", &v) && v > 0) t.group_m = v;
+  if (num("SP24_C_EVICT", &v)) t.c_evict = v != 0;
+  if (num("SP24_SPLITS", &v)) t.splits = v;
+  if (num("SP24_KROT", &v)) t.krot = v != 0;
+  if (num("SP24_PAIR_FINE", &v)) t.pair_fine = v != 0;
+  if (const char* k = std::getenv("SP24_KERNEL")) {
+    t.kernel_set = 1;
+    t.kernel = std::strcmp(k, "1sm") == 0      ? 1
+               : std::strcmp(k, "2sm") == 0    ? 2
+               : std::strcmp(k, "splitk") == 0 ? 3
+                                               : 0;
+  }
+  if (num("SP24_NARROW_PAIR", &v)) t.narrow_pair = v;
+  if (num("SP24_PAIR_SPLITK", &v)) t.pair_splitk = v;
+  if (num("SP24_PAIR_SPLITK_WIDTH", &v) && (v == 64 || v == 128)) t.pair_splitk_width = v;
+  if (num("SP24_SPLITK_B8", &v)) t.splitk_b8 = v != 0;
+  if (num("SP24_SPLITK_KB", &v) && (v == 1 || v == 2)) t.splitk_kb = v;
+  if (num("SP24_GATED", &v)) t.gated = v;
+  if (std::getenv("SP24_PAIR_GATED") != nullptr) t.pair_gated = 0;
+  return t;
+}
+
+std::mutex g_tuning_mu;
+bool g_tuning_loaded = false;
+Tuning g_tuning;
+
+Tuning tuning() {
+  std::lock_guard<std::mutex> lk(g_tuning_mu);
+  if (!g_tuning_loaded) {
+    g_tuning = read_tuning();
+    g_tuning_loaded = true;
+  }
+  return g_tuning;
+}
+
+// Sets a kernel's function attributes (dynamic shared memory, and the
+// non-portable cluster size when asked) once per device.  `done` is the
+// calling launcher's own per-device flag array; the first calls on a device
+// from several host threads serialise on the mutex.
+std::mutex g_attr_mu;
+
+template <typename Kern>
+sp24_status ensure_kernel_attrs(Kern kern, std::atomic<bool> (&done)[kMaxDevices], int smem,
+                                bool nonportable_cluster = false) {
+  int dev = 0;
+  SP24_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return SP24_ERR_ARG;
+  if (done[dev].load(std::memory_order_acquire)) return SP24_OK;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (done[dev].load(std::memory_order_relaxed)) return SP24_OK;
+  SP24_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  if (nonportable_cluster)
+    SP24_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  done[dev].store(true, std::memory_order_release);
+  return SP24_OK;
+}
+
 // Everything a launch needs after validation / workspace staging.
 struct Prepared {
   sp24_dtype dt;
@@ -176,11 +267,13 @@ struct Prepared {
   float alpha_up;
   const float* bias_up;
   int gate_from_c;
+  int c_reread;         // C is read back by a later launch (two-pass gated): keep it in L2
   sp24::PeerOut peers;
   int static_weights;   // SP24_HINT_STATIC_WEIGHTS in effect (narrow-N kernel)
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
+  Tuning tune;          // the tuning switches in effect for this call
 };
 
 // GEMM launches carry programmatic stream serialization: the kernel may be
@@ -188,14 +281,9 @@ struct Prepared {
 // prologue (barriers, TMEM allocation, tensor-map prefetch), and its TMA
 // producers wait for the previous grid (griddepcontrol.wait) before the
 // first load.  SP24_PDL=0 launches without the attribute.
-bool pdl_enabled() {
-  const char* env = std::getenv("SP24_PDL");
-  return env == nullptr || std::atoi(env) != 0;
-}
-
 template <typename... KArgs, typename... Args>
 sp24_status launch_gemm_kernel(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
-                               cudaStream_t stream, unsigned cluster, Args&&... args) {
+                               cudaStream_t stream, unsigned cluster, bool pdl, Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(block);
@@ -210,7 +298,7 @@ sp24_status launch_gemm_kernel(void (*kern)(KArgs...), unsigned grid, unsigned b
     attr[na].val.clusterDim.z = 1;
     ++na;
   }
-  if (pdl_enabled()) {
+  if (pdl) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -225,14 +313,9 @@ template <int DT, int BN>
 sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
   using C = sp24::GemmCfg<DT, BN>;
   auto kern = sp24::sp24_gemm_kernel<DT, BN>;
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  SP24_CUDA_TRY(cudaGetDevice(&dev));
-  if (!attr_set[dev]) {
-    SP24_CUDA_TRY(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const sp24_status ast = ensure_kernel_attrs(kern, attr_set, C::SMEM_BYTES);
+  if (ast != SP24_OK) return ast;
   const CUtensorMapDataType tdt =
       C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   CUtensorMap ta, tb;
@@ -273,17 +356,10 @@ sp24_status launch_gemm(const Prepared& p, const DeviceInfo& di, cudaStream_t st
   P.stall_producer = p.stall_producer;
   const int grid = std::min(P.num_tiles, di.sm_count);
   return launch_gemm_kernel(kern, static_cast<unsigned>(grid), sp24::kThreads, C::SMEM_BYTES, stream,
-                            0, ta, tb, P);
+                            0, p.tune.pdl != 0, ta, tb, P);
 }
 
 
-// Tile rasterisation group (M tiles walked together); SP24_GROUP_M overrides
-// for tuning runs.
-int group_m_env(int dflt) {
-  const char* env = std::getenv("SP24_GROUP_M");
-  const int v = env ? std::atoi(env) : 0;
-  return v > 0 ? v : dflt;
-}
 
 // Parameter block shared by the CTA-pair kernels; tiles of tile_m x tile_n.
 sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n) {
@@ -296,7 +372,7 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
   P.n_tiles = (p.n + tile_n - 1) / tile_n;
   P.k_stages = (p.k + bkd - 1) / bkd;
   P.num_tiles = P.m_pairs * P.n_tiles;
-  P.group_m = group_m_env(8);
+  P.group_m = p.tune.group_m > 0 ? p.tune.group_m : 8;
   P.splits = 1;
   P.c_f32 = p.c_f32;
   P.c_bf16 = static_cast<__nv_bfloat16*>(p.c_bf16);
@@ -319,12 +395,12 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
                                                             : 0;
   // C under an L2 evict-first policy, so the output does not push the A and B
   // tiles that other CTAs still read out of L2 (configuration 2, fp32 + bf16
-  // out: +1%).  The fused all-gather and the second gated pass read C back
-  // and keep the default policy.  SP24_C_EVICT=0 turns it off.
-  const char* cev = std::getenv("SP24_C_EVICT");
-  P.c_evict_first = ((cev == nullptr || std::atoi(cev) != 0) && p.peers.n == 0 && !p.gate_from_c)
-                        ? 1
-                        : 0;
+  // out: +1%).  Outputs that are read back keep the default policy: the fused
+  // all-gather re-reads its stores, the first gated pass writes the
+  // intermediate that the second pass reads, and the second pass reads C
+  // itself.  SP24_C_EVICT=0 turns it off.
+  P.c_evict_first =
+      (p.tune.c_evict && p.peers.n == 0 && !p.gate_from_c && !p.c_reread) ? 1 : 0;
   P.status = p.status;
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
@@ -342,14 +418,9 @@ template <int DT, int FINE, int BNP = 256, int G = 1>
 sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
   using C = sp24::PairCfg<DT, FINE, BNP, G>;
   auto kern = sp24::sp24_gemm2sm_kernel<DT, FINE, BNP, G>;
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  SP24_CUDA_TRY(cudaGetDevice(&dev));
-  if (!attr_set[dev]) {
-    SP24_CUDA_TRY(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const sp24_status ast = ensure_kernel_attrs(kern, attr_set, C::SMEM_BYTES);
+  if (ast != SP24_OK) return ast;
   const CUtensorMapDataType tdt =
       C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   CUtensorMap ta, tb, te;
@@ -378,7 +449,7 @@ sp24_status launch_gemm2sm(const Prepared& p, const DeviceInfo& di, cudaStream_t
   const int pairs = std::max(1, std::min(P.num_tiles, di.sm_count / 2));
   // Cluster shape (2) comes from the kernel's __cluster_dims__.
   return launch_gemm_kernel(kern, static_cast<unsigned>(2 * pairs), sp24::kPairThreads,
-                            C::SMEM_BYTES, stream, 0, ta, tb, te, ta2, te2, P);
+                            C::SMEM_BYTES, stream, 0, p.tune.pdl != 0, ta, tb, te, ta2, te2, P);
 }
 
 // Largest cluster of split-K CTAs the device keeps resident `tiles` times
@@ -427,9 +498,7 @@ int max_active_clusters(Kern kern, int smem, int csize, int family = 0,
 // lowered until all clusters are resident at once.  SP24_SPLITS overrides
 // (tests and tuning runs; still clamped to those limits).
 template <typename Kern>
-int choose_splits(Kern kern, int smem, int tiles, int stages, int sm_count) {
-  const char* env = std::getenv("SP24_SPLITS");
-  const int forced = env ? std::atoi(env) : 0;
+int choose_splits(Kern kern, int smem, int tiles, int stages, int sm_count, int forced) {
   int s = forced > 0 ? forced : (tiles * 4 >= sm_count * 3 ? 1 : sm_count / tiles);
   s = std::min(s, sp24::kMaxSplits);
   s = std::min(s, std::max(1, forced > 0 ? stages : stages / 2));
@@ -446,15 +515,9 @@ sp24_status launch_gemm2sm_splitk(const Prepared& p, const DeviceInfo& di, cudaS
                                   int splits) {
   using C = sp24::PairCfg<DT, 0, BNP>;
   auto kern = sp24::sp24_gemm2sm_splitk_kernel<DT, BNP>;
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  SP24_CUDA_TRY(cudaGetDevice(&dev));
-  if (!attr_set[dev]) {
-    SP24_CUDA_TRY(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    SP24_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const sp24_status ast = ensure_kernel_attrs(kern, attr_set, C::SMEM_BYTES, true);
+  if (ast != SP24_OK) return ast;
   const CUtensorMapDataType tdt =
       C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   CUtensorMap ta, tb, te;
@@ -478,21 +541,16 @@ sp24_status launch_gemm2sm_splitk(const Prepared& p, const DeviceInfo& di, cudaS
   P.splits = splits;
   return launch_gemm_kernel(kern, static_cast<unsigned>(P.num_tiles * 2 * splits),
                             sp24::kPairThreads, C::SMEM_BYTES, stream,
-                            static_cast<unsigned>(2 * splits), ta, tb, te, P);
+                            static_cast<unsigned>(2 * splits), p.tune.pdl != 0, ta, tb, te, P);
 }
 
 template <int DT, int BN, int KB, int G>
 sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t stream) {
   using C = sp24::SplitCfg<DT, BN, KB, G>;
   auto kern = sp24::sp24_gemm_splitk_kernel<DT, BN, KB, G>;
-  static bool attr_set[kMaxDevices] = {};
-  int dev = 0;
-  SP24_CUDA_TRY(cudaGetDevice(&dev));
-  if (!attr_set[dev]) {
-    SP24_CUDA_TRY(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    attr_set[dev] = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const sp24_status ast = ensure_kernel_attrs(kern, attr_set, C::SMEM_BYTES);
+  if (ast != SP24_OK) return ast;
   const CUtensorMapDataType tdt =
       C::ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
   CUtensorMap ta, tb;
@@ -538,34 +596,29 @@ sp24_status launch_splitk(const Prepared& p, const DeviceInfo& di, cudaStream_t 
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
   P.static_weights = p.static_weights;
-  const char* krot = std::getenv("SP24_KROT");   // 0: every tile in K order (tuning runs)
-  P.rotate = (krot == nullptr || std::atoi(krot) != 0) ? 1 : 0;
+  P.rotate = p.tune.krot;   // SP24_KROT=0: every tile in K order (tuning runs)
   P.meta_up = p.meta_up;
   P.alpha_up = p.alpha_up;
   P.bias_up = p.bias_up;
   const int tiles = P.m_blocks * P.n_tiles;
-  P.splits = choose_splits(kern, C::SMEM_BYTES, tiles, P.stages, di.sm_count);
+  P.splits = choose_splits(kern, C::SMEM_BYTES, tiles, P.stages, di.sm_count, p.tune.splits);
 
   // Launched with an explicit cluster shape of S CTAs, S = 1 included.
   return launch_gemm_kernel(kern, static_cast<unsigned>(tiles * P.splits), sp24::kThreads,
-                            C::SMEM_BYTES, stream, static_cast<unsigned>(P.splits), ta, tb, ta2, P);
+                            C::SMEM_BYTES, stream, static_cast<unsigned>(P.splits), p.tune.pdl != 0,
+                            ta, tb, ta2, P);
 }
 
 // Stage granularity of the CTA-pair kernel (PairCfg FINE); SP24_PAIR_FINE=0|1
 // overrides for tuning runs.
-bool pair_fine_stages() {
-  const char* env = std::getenv("SP24_PAIR_FINE");
-  if (env != nullptr) return std::atoi(env) != 0;
-  return false;
-}
+bool pair_fine_stages(const Tuning& t) { return t.pair_fine != 0; }
 
 // Kernel choice: the CTA-pair kernel for problems with at least one full
 // 256 x 256 tile, the single-CTA kernel (narrow N tiles) otherwise.
 // SP24_KERNEL=1sm|2sm overrides (benchmarks and tests).
-bool use_pair_kernel(int m, int n, int hint) {
-  const char* env = std::getenv("SP24_KERNEL");
-  if (env != nullptr && std::strcmp(env, "1sm") == 0) return false;
-  if (env != nullptr && std::strcmp(env, "2sm") == 0) return true;
+bool use_pair_kernel(int m, int n, int hint, const Tuning& t) {
+  if (t.kernel == 1) return false;
+  if (t.kernel == 2) return true;
   if (hint != 0 && hint != 256) return false;
   return m >= 256 && n >= 256;
 }
@@ -578,12 +631,10 @@ bool use_pair_kernel(int m, int n, int hint) {
 // streams a full B per tile and is latency-bound there (W_up, T = 128).
 // Returns the tile width or 0.  SP24_NARROW_PAIR=0 turns it off, =1 forces it
 // for every eligible shape (tests and tuning runs).
-int narrow_pair_width(const sp24_gemm_desc* d, int sm_count) {
-  const char* env = std::getenv("SP24_NARROW_PAIR");
-  const int mode = env != nullptr ? std::atoi(env) : -1;
+int narrow_pair_width(const sp24_gemm_desc* d, int sm_count, const Tuning& t) {
+  const int mode = t.narrow_pair;
   if (mode == 0) return 0;
-  const char* kern = std::getenv("SP24_KERNEL");
-  if (kern != nullptr && mode != 1) return 0;   // a forced kernel choice wins
+  if (t.kernel_set && mode != 1) return 0;   // a forced kernel choice wins
   if (d->tile_n != 0 || d->n > 128) return 0;
   // 32-wide tiles stage 16 columns (32 B rows) per CTA: 16-bit types only.
   if (d->n <= 32 && is_fp8(d->dtype)) return 0;
@@ -603,17 +654,14 @@ int narrow_pair_width(const sp24_gemm_desc* d, int sm_count) {
 // that 2 S CTAs per tile occupy most of the SMs.  Returns the tile width or
 // 0.  SP24_PAIR_SPLITK=0 turns it off; =S forces S pairs on every eligible
 // shape (tests and tuning runs).
-int narrow_pair_splitk_width(const sp24_gemm_desc* d, int sm_count, int* splits) {
-  const char* env = std::getenv("SP24_PAIR_SPLITK");
-  const int forced = env != nullptr ? std::atoi(env) : -1;
+int narrow_pair_splitk_width(const sp24_gemm_desc* d, int sm_count, int* splits,
+                             const Tuning& t) {
+  const int forced = t.pair_splitk;
   if (forced == 0) return 0;
-  const char* kern = std::getenv("SP24_KERNEL");
-  if (kern != nullptr && forced < 1) return 0;   // a forced kernel choice wins
+  if (t.kernel_set && forced < 1) return 0;   // a forced kernel choice wins
   if (d->tile_n != 0 || d->n > 128 || d->n <= (is_fp8(d->dtype) ? 32 : 16)) return 0;
   int np = d->n <= 32 ? 32 : d->n <= 64 ? 64 : 128;
-  const char* wenv = std::getenv("SP24_PAIR_SPLITK_WIDTH");   // tuning: 64 or 128
-  if (wenv != nullptr && (std::atoi(wenv) == 64 || std::atoi(wenv) == 128) && d->n > 32)
-    np = std::atoi(wenv);
+  if (t.pair_splitk_width != 0 && d->n > 32) np = t.pair_splitk_width;   // tuning: 64 or 128
   if (forced >= 1) {
     *splits = std::min(forced, 4);
     return np;
@@ -630,11 +678,10 @@ int narrow_pair_splitk_width(const sp24_gemm_desc* d, int sm_count, int* splits)
 // K splitting win.  With thousands of narrow tiles the persistent
 // single-CTA kernel, whose grouped tile order shares operands in L2, is
 // faster.  SP24_KERNEL=1sm|splitk overrides.
-bool use_splitk_kernel(int m, int n, int bn, int sm_count) {
-  const char* env = std::getenv("SP24_KERNEL");
-  if (env != nullptr && std::strcmp(env, "1sm") == 0) return false;
+bool use_splitk_kernel(int m, int n, int bn, int sm_count, const Tuning& t) {
+  if (t.kernel == 1) return false;
   if (bn > 128) return false;
-  if (env != nullptr && std::strcmp(env, "splitk") == 0) return true;
+  if (t.kernel == 3) return true;
   const long long tiles = static_cast<long long>((m + 127) / 128) * ((n + bn - 1) / bn);
   return n <= 128 || tiles <= 4LL * sm_count;
 }
@@ -642,18 +689,15 @@ bool use_splitk_kernel(int m, int n, int bn, int sm_count) {
 // Split-K tile width for a 16-column choice: 8 for 16-bit types with at most
 // 8 columns, whose 16-column B boxes would be half outside B (the kernel's
 // 8-column form loads in-bounds boxes only).  SP24_SPLITK_B8=0 turns it off.
-int splitk_tile_n(const sp24_gemm_desc* d, int bn) {
+int splitk_tile_n(const sp24_gemm_desc* d, int bn, const Tuning& t) {
   if (bn != 16 || d->n > 8 || is_fp8(d->dtype)) return bn;
-  const char* env = std::getenv("SP24_SPLITK_B8");
-  return (env != nullptr && std::atoi(env) == 0) ? bn : 8;
+  return t.splitk_b8 ? 8 : bn;
 }
 
 // Units per split-K stage: two (32 KB of A_c) for tiles up to 32 wide, one
 // above, where B's share of a stage grows.  SP24_SPLITK_KB=1|2 overrides.
-int splitk_units(int bn) {
-  const char* env = std::getenv("SP24_SPLITK_KB");
-  const int v = env ? std::atoi(env) : 0;
-  if (v == 1 || v == 2) return v;
+int splitk_units(int bn, const Tuning& t) {
+  if (t.splitk_kb != 0) return t.splitk_kb;
   return bn <= 32 ? 2 : 1;
 }
 
@@ -685,12 +729,12 @@ LaunchFn pick_narrow_pair(int np) {
 // Pair-kernel variant: the 256 x 256 tile with coarse stages, or its
 // fine-staged form (SP24_PAIR_FINE=1).
 template <int DT>
-LaunchFn pick_pair_dt() {
-  return pair_fine_stages() ? launch_gemm2sm<DT, 1> : launch_gemm2sm<DT, 0>;
+LaunchFn pick_pair_dt(const Tuning& t) {
+  return pair_fine_stages(t) ? launch_gemm2sm<DT, 1> : launch_gemm2sm<DT, 0>;
 }
 
-LaunchFn pick_pair(sp24_dtype dt) {
-  return dt == SP24_F16 ? pick_pair_dt<0>() : dt == SP24_BF16 ? pick_pair_dt<1>() : pick_pair_dt<2>();
+LaunchFn pick_pair(sp24_dtype dt, const Tuning& t) {
+  return dt == SP24_F16 ? pick_pair_dt<0>(t) : dt == SP24_BF16 ? pick_pair_dt<1>(t) : pick_pair_dt<2>(t);
 }
 
 template <int DT>
@@ -894,6 +938,7 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
   p.stall_producer = stall;
   p.static_weights =
       (g_launch_hints & SP24_HINT_STATIC_WEIGHTS) != 0 && d->meta_format == SP24_META_TC ? 1 : 0;
+  p.tune = tuning();
 
   if (d->meta_format == SP24_META_REF) {
     st = sp24_repack_meta(d->dtype, d->meta, d->m, d->k, ws + w.meta_off,
@@ -932,16 +977,15 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     const int bn = std::min(128, choose_bn(d->m, d->n, d->tile_n, di->sm_count));
     const long long tiles = static_cast<long long>((d->m + 127) / 128) * ((d->n + bn - 1) / bn);
     int pks = 0;
+    const Tuning& t = p.tune;
     const bool pairs_narrow = d->n > 64 && d->n <= 128 &&
-                              (narrow_pair_width(d, di->sm_count) > 0 ||
-                               narrow_pair_splitk_width(d, di->sm_count, &pks) > 0);
-    const char* genv = std::getenv("SP24_GATED");
-    const int gmode = genv != nullptr ? std::atoi(genv) : 0;
+                              (narrow_pair_width(d, di->sm_count, t) > 0 ||
+                               narrow_pair_splitk_width(d, di->sm_count, &pks, t) > 0);
+    const int gmode = t.gated;
     const bool one_launch = gmode == 1 || (gmode != 2 && !pairs_narrow &&
                                            (d->n <= 128 || tiles <= 4LL * di->sm_count));
-    const int npg = narrow_pair_width(d, di->sm_count);
-    if (gmode != 1 && gmode != 2 && npg >= 64 && d->n > 32 &&
-        std::getenv("SP24_PAIR_GATED") == nullptr) {
+    const int npg = narrow_pair_width(d, di->sm_count, t);
+    if (gmode != 1 && gmode != 2 && npg >= 64 && d->n > 32 && t.pair_gated) {
       // 1: W_gate and W_up against the same B stages of a CTA pair.
       LaunchFn pg = d->dtype == SP24_F16    ? pick_pair_gated<0>(npg)
                     : d->dtype == SP24_BF16 ? pick_pair_gated<1>(npg)
@@ -950,7 +994,7 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     }
     if (one_launch) {
       // 2: both weights through the split-K kernel's ring.
-      const int sbn = splitk_tile_n(d, bn);
+      const int sbn = splitk_tile_n(d, bn, t);
       LaunchFn gf = d->dtype == SP24_F16    ? pick_gated<0>(sbn)
                     : d->dtype == SP24_BF16 ? pick_gated<1>(sbn)
                                             : pick_gated<2>(sbn);
@@ -962,6 +1006,7 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
     // epilogue and writes the result.
     Prepared p1 = p;
     p1.a_c_up = nullptr;
+    p1.c_reread = 1;
     if (p1.c_f32 != nullptr) p1.c_bf16 = nullptr;
     st = launch_plain(d, p1, *di, stream);
     if (st != SP24_OK) return st;
@@ -983,11 +1028,12 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
 sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const DeviceInfo& di_ref,
                          cudaStream_t stream) {
   const DeviceInfo* di = &di_ref;
-  if (use_pair_kernel(d->m, d->n, d->tile_n)) {
-    return pick_pair(d->dtype)(p, *di, stream);
+  const Tuning& t = p.tune;
+  if (use_pair_kernel(d->m, d->n, d->tile_n, t)) {
+    return pick_pair(d->dtype, t)(p, *di, stream);
   }
   const int bn = choose_bn(d->m, d->n, d->tile_n, di->sm_count);
-  const int np = narrow_pair_width(d, di->sm_count);
+  const int np = narrow_pair_width(d, di->sm_count, t);
   if (np > 0) {
     LaunchFn nf = d->dtype == SP24_F16    ? pick_narrow_pair<0>(np)
                   : d->dtype == SP24_BF16 ? pick_narrow_pair<1>(np)
@@ -995,15 +1041,15 @@ sp24_status launch_plain(const sp24_gemm_desc* d, const Prepared& p, const Devic
     return nf(p, *di, stream);
   }
   int pks = 0;
-  const int npk = narrow_pair_splitk_width(d, di->sm_count, &pks);
+  const int npk = narrow_pair_splitk_width(d, di->sm_count, &pks, t);
   if (npk > 0) {
     return d->dtype == SP24_F16    ? pick_pair_splitk<0>(npk)(p, *di, stream, pks)
            : d->dtype == SP24_BF16 ? pick_pair_splitk<1>(npk)(p, *di, stream, pks)
                                    : pick_pair_splitk<2>(npk)(p, *di, stream, pks);
   }
-  if (use_splitk_kernel(d->m, d->n, bn, di->sm_count)) {
-    const int kb = splitk_units(bn);
-    const int sbn = splitk_tile_n(d, bn);
+  if (use_splitk_kernel(d->m, d->n, bn, di->sm_count, t)) {
+    const int kb = splitk_units(bn, t);
+    const int sbn = splitk_tile_n(d, bn, t);
     LaunchFn sf = d->dtype == SP24_F16    ? pick_splitk<0>(sbn, kb)
                   : d->dtype == SP24_BF16 ? pick_splitk<1>(sbn, kb)
                                           : pick_splitk<2>(sbn, kb);
@@ -1090,8 +1136,7 @@ sp24_status sp24_gemm(const sp24_gemm_desc* d, sp24_stream_t stream) {
   return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0);
 }
 
-// Allocation-free sp24_gemm: the scratch sp24_gemm would take from
-// d->workspace comes from the fixed device buffer g_sp24_noalloc_scratch.
+// sp24_gemm with a fused epilogue (bias, SiLU, or the gated SwiGLU form).
 sp24_status sp24_gemm_fused(const sp24_gemm_desc* d, const sp24_epilogue* e,
                             sp24_stream_t stream) {
   return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0, e);
@@ -1133,6 +1178,8 @@ sp24_status sp24_ipc_close(void* base) {
   return SP24_OK;
 }
 
+// Allocation-free sp24_gemm: the scratch sp24_gemm would take from
+// d->workspace comes from the fixed device buffer g_sp24_noalloc_scratch.
 sp24_status sp24_gemm_noalloc(const sp24_gemm_desc* d, sp24_stream_t stream) {
   sp24_status st = validate(d);
   if (st != SP24_OK) return st;
@@ -1165,6 +1212,13 @@ sp24_status sp24_selftest_timeout(const sp24_gemm_desc* d, unsigned long long ti
 }
 
 void sp24_set_launch_hints(unsigned hints) { g_launch_hints = hints; }
+
+void sp24_reload_tuning(void) {
+  const Tuning t = read_tuning();
+  std::lock_guard<std::mutex> lk(g_tuning_mu);
+  g_tuning = t;
+  g_tuning_loaded = true;
+}
 
 unsigned sp24_get_launch_hints(void) { return g_launch_hints; }
 

@@ -159,13 +159,24 @@ SP24_DEV void st_global_v8_u32(void* p, const uint32_t* v) {
 
 template <int CW>
 SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
-                                const uint32_t (&r)[CW], int row, int col0);
+                                uint32_t (&r)[CW], int row, int col0);
+template <int CW>
+SP24_DEV void pair_epilogue_row(const PairParams& P, uint32_t (&r)[CW], int row, int col0);
 
 // Store CW consecutive accumulator columns of one row (already in registers).
+// Warp-collective: every lane of the warp calls it (lane i holding row
+// row0 + i); lanes whose row is beyond M compute nothing and store nothing.
 template <int CW>
 SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[CW], int row, int col0) {
-  if (row >= P.m) return;
-  // The epilogue is applied in place, so the stores below see final values.
+  if (row < P.m) pair_epilogue_row<CW>(P, r, row, col0);
+  pair_store_row_to<CW>(P, P.c_f32, P.c_bf16, r, row, col0);
+}
+
+// The epilogue of one row, in place on its registers: alpha, bias and the
+// activation, then (second pass of a two-pass gated epilogue) the product
+// with the value already in C.
+template <int CW>
+SP24_DEV void pair_epilogue_row(const PairParams& P, uint32_t (&r)[CW], int row, int col0) {
   if (P.bias != nullptr || P.act != kActNone) {
     const bool hb = P.bias != nullptr;
     const float b = hb ? P.bias[row] : 0.0f;
@@ -177,7 +188,6 @@ SP24_DEV void pair_store_row(const PairParams& P, uint32_t (&r)[CW], int row, in
     for (int i = 0; i < CW; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * P.alpha);
   }
   if (P.gate_from_c) gate_mul_row<CW>(P, reinterpret_cast<float*>(r), row, col0);
-  pair_store_row_to<CW>(P, P.c_f32, P.c_bf16, r, row, col0);
 }
 
 // Fused all-gather, warp-cooperative: after a warp has stored its 32 rows x
@@ -226,37 +236,125 @@ SP24_DEV void pair_push_rows_to_peers(const PairParams& P, int row0, int col0) {
   }
 }
 
-// Stores CW finished values of one row (as float bits) into one copy of C.
-template <int CW>
-SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
-                                const uint32_t (&r)[CW], int row, int col0) {
-  const bool full = col0 + CW <= P.n;
-  const uint64_t pol = P.c_evict_first ? l2_evict_first_policy() : 0;
-  if (c32 != nullptr) {
-    float* dst = c32 + static_cast<long long>(row) * P.ldc + col0;
-    if (full && P.vec_f32 == 2) {
+// 4 x 4 transpose of 32-byte units inside each group of four lanes: unit j
+// (u[8j .. 8j+7]) of lane 4g+i moves to unit i of lane 4g+j.  Two butterfly
+// stages (lane bit 0, then bit 1), 16 shuffles each.  Afterwards unit q of
+// lane 4g+p holds what was unit p of lane 4g+q, so when lane 4g+p stores its
+// unit q to row (4g+q) at byte offset 32p, the four lanes of a group write
+// one 128-byte run of one row.
+SP24_DEV void quad_transpose_units(uint32_t (&u)[32]) {
+  const int p = threadIdx.x & 3;
 #pragma unroll
-      for (int i = 0; i < CW; i += 8) {
-        float v[8];
+  for (int m = 1; m <= 2; m <<= 1) {
+    const bool hi = (p & m) != 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]);
-        if (P.c_evict_first)
-          st_global_v8_hint(dst + i, v, pol);
+    for (int j = 0; j < 4; ++j) {
+      if (j & m) continue;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t send = hi ? u[8 * j + e] : u[8 * (j + m) + e];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
+        if (hi)
+          u[8 * j + e] = recv;
         else
-          st_global_v8(dst + i, v);
+          u[8 * (j + m) + e] = recv;
       }
-    } else if (full && P.vec_f32 == 1) {
-#pragma unroll
-      for (int i = 0; i < CW; i += 4)
-        *reinterpret_cast<float4*>(dst + i) =
-            make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
-                        __uint_as_float(r[i + 3]));
-    } else {
-#pragma unroll
-      for (int i = 0; i < CW; ++i)
-        if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]);
     }
   }
+}
+
+// Warp-collective store of 128-byte row runs: each lane holds 32 words of
+// its own row (lane i: row row0 + i, bytes [0, 128) of the run at `base` +
+// row * pitch); after the quad transpose every store instruction writes 8
+// whole 128-byte runs (rows 4g + q for the 8 groups g) instead of 32
+// scattered 32-byte pieces, a quarter of the L2 write requests.
+SP24_DEV void store_rows_128b(void* base, long long pitch_bytes, uint32_t (&u)[32], int row0,
+                              int m, bool evict_first, uint64_t pol) {
+  quad_transpose_units(u);
+  const int lane = threadIdx.x & 31;
+  const int p = lane & 3, g = lane >> 2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int row = row0 + 4 * g + q;
+    if (row < m) {
+      uint8_t* dst = static_cast<uint8_t*>(base) + static_cast<long long>(row) * pitch_bytes + 32 * p;
+      if (evict_first)
+        st_global_v8_u32_hint(dst, &u[8 * q], pol);
+      else
+        st_global_v8_u32(dst, &u[8 * q]);
+    }
+  }
+}
+
+// Stores CW finished values of one row (as float bits) into one copy of C.
+// Warp-collective (see pair_store_row); r may be reordered on return.
+// With 32-byte aligned rows the stores go through the quad transpose:
+//   fp32 out:   each 32-column chunk of r is transposed in place and stored
+//               as 128-byte runs; a bf16 copy is then converted from the
+//               transposed registers, unit by unit, and stored as 64-byte
+//               runs (16 bytes per lane);
+//   bf16 only:  each 64-column chunk is packed to bf16 pairs in place,
+//               transposed and stored as 128-byte runs.
+// Narrow or ragged tiles and less aligned outputs store per lane.
+template <int CW>
+SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* c16,
+                                uint32_t (&r)[CW], int row, int col0) {
+  const bool full = col0 + CW <= P.n;   // warp-uniform: one column range per warp
+  const bool live = row < P.m;
+  const bool ef = P.c_evict_first != 0;
+  const uint64_t pol = ef ? l2_evict_first_policy() : 0;
+  const int row0 = row - static_cast<int>(threadIdx.x & 31);
+  const bool t32 = c32 != nullptr && full && P.vec_f32 == 2 && CW % 32 == 0 &&
+                   (c16 == nullptr || P.vec_bf16 >= 1);
+  const bool t16 = c32 == nullptr && c16 != nullptr && full && P.vec_bf16 == 2 && CW % 64 == 0;
+  if (t32) {
+    const int lane = threadIdx.x & 31;
+    const int p = lane & 3, g = lane >> 2;
+#pragma unroll
+    for (int c = 0; c < CW; c += 32) {
+      uint32_t(&u)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[c]);
+      store_rows_128b(c32 + col0 + c, P.ldc * 4, u, row0, P.m, ef, pol);
+      if (c16 != nullptr) {
+        // Unit q now holds row 4g+q, columns c + 8p .. c + 8p + 7.
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(u[8 * q + 2 * e]),
+                                                     __uint_as_float(u[8 * q + 2 * e + 1]));
+            pk[e] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          const int rr = row0 + 4 * g + q;
+          if (rr < P.m) {
+            __nv_bfloat16* dst = c16 + static_cast<long long>(rr) * P.ldc + col0 + c + 8 * p;
+            if (ef)
+              st_global_v4_u32_hint(dst, pk, pol);
+            else
+              *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (t16) {
+#pragma unroll
+    for (int c = 0; c < CW; c += 64) {
+      // bf16 pairs packed in place into r[c .. c+31] (each word is written
+      // after the two values it replaces have been read).
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[c + 2 * j]),
+                                                 __uint_as_float(r[c + 2 * j + 1]));
+        r[c + j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      store_rows_128b(c16 + col0 + c, P.ldc * 2, *reinterpret_cast<uint32_t(*)[32]>(&r[c]), row0,
+                      P.m, ef, pol);
+    }
+    return;
+  }
+  if (!live) return;
   if (c16 != nullptr) {
     __nv_bfloat16* dst = c16 + static_cast<long long>(row) * P.ldc + col0;
     if (full && P.vec_bf16 >= 1) {
@@ -270,7 +368,7 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
           pk[j] = *reinterpret_cast<uint32_t*>(&h);
         }
         if (P.vec_bf16 == 2) {
-          if (P.c_evict_first)
+          if (ef)
             st_global_v8_u32_hint(dst + i, pk, pol);
           else
             st_global_v8_u32(dst + i, pk);
@@ -283,6 +381,31 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
 #pragma unroll
       for (int i = 0; i < CW; ++i)
         if (col0 + i < P.n) dst[i] = __float2bfloat16_rn(__uint_as_float(r[i]));
+    }
+  }
+  if (c32 != nullptr) {
+    float* dst = c32 + static_cast<long long>(row) * P.ldc + col0;
+    if (full && P.vec_f32 == 2) {
+#pragma unroll
+      for (int i = 0; i < CW; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[i + j]);
+        if (ef)
+          st_global_v8_hint(dst + i, v, pol);
+        else
+          st_global_v8(dst + i, v);
+      }
+    } else if (full && P.vec_f32 == 1) {
+#pragma unroll
+      for (int i = 0; i < CW; i += 4)
+        *reinterpret_cast<float4*>(dst + i) =
+            make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                        __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < CW; ++i)
+        if (col0 + i < P.n) dst[i] = __uint_as_float(r[i]);
     }
   }
 }
@@ -578,8 +701,8 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
             r[c] = __float_as_uint(
                 epi_value(__uint_as_float(r[c]), P.alpha, bg, hg, P.act) *
                 epi_value(__uint_as_float(ru[c]), P.alpha_up, bu, hu, kActNone));
-          pair_store_row_to<C::CW>(P, P.c_f32, P.c_bf16, r, row, nb * C::BN + half * C::CW);
         }
+        pair_store_row_to<C::CW>(P, P.c_f32, P.c_bf16, r, row, nb * C::BN + half * C::CW);
         aph ^= 1u;
         continue;
       }

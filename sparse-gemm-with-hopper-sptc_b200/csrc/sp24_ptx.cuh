@@ -443,6 +443,13 @@ SP24_DEV void st_global_v8_u32_hint(void* p, const uint32_t* v, uint64_t pol) {
                : "memory");
 }
 
+// 16-byte global store under an L2 cache policy.
+SP24_DEV void st_global_v4_u32_hint(void* p, const uint32_t* v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "l"(pol)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 format):
 //   [0,14) start address >> 4, [16,30) leading byte offset >> 4,

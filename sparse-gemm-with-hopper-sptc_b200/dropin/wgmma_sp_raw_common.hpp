@@ -17,9 +17,15 @@
 // (sp24_compress, checked bit-for-bit against the host compression) and runs
 // the GEMM through sp24_gemm (tcgen05.mma.sp) instead of the sm_90a wgmma
 // kernel.  The device gate is sm_100 instead of sm_90.
+//   * wgmma_sp_raw_kernel<Element, BlockN> (:955-1030) stays launchable with
+//     the reference's signature and <<<dim3(n / BlockN, m / 64), 128>>>
+//     geometry, for callers that launch it themselves: sp24_raw_kernel.cuh,
+//     a tcgen05.mma.sp kernel of that shape (sp24_gemm, with its persistent
+//     warp-specialised kernels, is the fast path).
 #pragma once
 
 #include "sp24_host_utils.hpp"
+#include "sp24_raw_kernel.cuh"
 
 // ------------------------------------------------------------------ configuration
 constexpr int kRawBlockM = 64;

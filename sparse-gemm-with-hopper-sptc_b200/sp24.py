@@ -19,6 +19,7 @@ from ctypes import (POINTER, Structure, c_char_p, c_float, c_int, c_int64, c_lon
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libsp24.so")
+PEAK_LIB_PATH = os.path.join(HERE, "lib", "libsp24_peak.so")
 
 F16, BF16, E4M3 = 0, 1, 2
 # Mixed fp8: A's format first, B's second (kind::f8f6f4 formats may differ).
@@ -39,7 +40,7 @@ EXPORTS = [
     "sp24_quantize_e4m3", "sp24_shard_columns", "sp24_unshard_columns_f32",
     "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused", "sp24_repack_meta_k16",
     "sp24_gemm_allgather", "sp24_ipc_get_handle", "sp24_ipc_open_handle", "sp24_ipc_close",
-    "sp24_set_launch_hints", "sp24_get_launch_hints",
+    "sp24_set_launch_hints", "sp24_get_launch_hints", "sp24_reload_tuning",
 ]
 MAX_PEERS = 7
 HINT_NONE, HINT_STATIC_WEIGHTS = 0, 1
@@ -109,6 +110,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_set_launch_hints.argtypes = [ctypes.c_uint]
     lib.sp24_set_launch_hints.restype = None
     lib.sp24_get_launch_hints.restype = ctypes.c_uint
+    lib.sp24_reload_tuning.restype = None
+    lib.sp24_reload_tuning.argtypes = []
     lib.sp24_compress.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
                                   c_void_p, c_void_p, POINTER(c_longlong), c_void_p]
     lib.sp24_prune_2of4.argtypes = [c_int, c_void_p, c_int, c_int, c_int64, c_void_p, c_int64,
@@ -342,6 +345,34 @@ def get_launch_hints() -> int:
     return load().sp24_get_launch_hints()
 
 
+def reload_tuning() -> None:
+    """sp24_reload_tuning: the library reads its SP24_* tuning variables once;
+    call this after changing them in os.environ."""
+    load().sp24_reload_tuning()
+
+
+class tuning_env:
+    """Context manager: set SP24_* tuning variables for the calls inside it
+    (and re-read them in the library), restoring the old values on exit."""
+
+    def __init__(self, env: dict):
+        self.env = {k: str(v) for k, v in env.items()}
+
+    def __enter__(self):
+        self.old = {k: os.environ.get(k) for k in self.env}
+        os.environ.update(self.env)
+        reload_tuning()
+        return self
+
+    def __exit__(self, *exc):
+        for k, v in self.old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+        reload_tuning()
+
+
 def last_kernel_status(stream=None) -> int:
     return int(load().sp24_last_kernel_status(_stream(stream)))
 
@@ -378,3 +409,30 @@ def unshard_columns_f32(src, m: int, n: int, world: int, align: int, stream=None
     _check(load().sp24_unshard_columns_f32(_ptr(src), _ptr(dst), m, n, world, align,
                                            _stream(stream)), "sp24_unshard_columns_f32")
     return dst
+
+
+_peak = None
+
+
+def probe_mma_rate(dtype: int, sparse: bool, iters: int = 4096, reps: int = 5, stream=None):
+    """Tensor-core rate of the CTA-pair MMA shape with operands resident in
+    shared memory (lib/libsp24_peak.so, measurement only): returns
+    (dense-equivalent TFLOP/s, ms per launch).  dtype: F16, BF16 or E4M3."""
+    global _peak
+    import torch
+    if _peak is None:
+        if not os.path.exists(PEAK_LIB_PATH):
+            raise FileNotFoundError(f"{PEAK_LIB_PATH} missing: run __graft_entry__.build() first")
+        _peak = ctypes.CDLL(PEAK_LIB_PATH)
+        _peak.sp24_probe_mma_rate.restype = c_int
+        _peak.sp24_probe_mma_rate.argtypes = [c_int, c_int, c_int, c_int, POINTER(c_float),
+                                              POINTER(ctypes.c_double), c_void_p, c_void_p]
+    ms, flops = c_float(0.0), ctypes.c_double(0.0)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _check(_peak.sp24_probe_mma_rate(dtype, 1 if sparse else 0, iters, reps, ctypes.byref(ms),
+                                     ctypes.byref(flops), _ptr(status), _stream(stream)),
+           "sp24_probe_mma_rate")
+    torch.cuda.synchronize()
+    if status.item() != 0:
+        raise Sp24Error(6, "sp24_probe_mma_rate")
+    return flops.value / (ms.value * 1e-3) / 1e12, ms.value

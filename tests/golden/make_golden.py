@@ -60,7 +60,11 @@ def alternating_a(dt: int, m: int, k: int):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-dir", default="/root/reference")
+    here = os.path.dirname(os.path.abspath(__file__))
+    default_ref = os.environ.get("SP24_REF_DIR",
+                                 os.path.join(here, "..", "..", "..", "reference"))
+    ap.add_argument("--ref-dir", default=os.path.normpath(default_ref),
+                    help="the reference checkout (SP24_REF_DIR, else ../reference beside the repo)")
     args = ap.parse_args()
     if not oracle.ref_available():
         sys.exit("oracle/_ref/libsp24ref.so missing: run `make -C oracle ref`")

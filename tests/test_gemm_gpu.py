@@ -55,6 +55,9 @@ def check_c(c_gpu, c_ref, a_bits, b_bits, dt, abs_rule=True):
 @pytest.fixture(autouse=True)
 def _clean_status():
     yield
+    # Tests that set tuning variables through monkeypatch have had them
+    # restored by now (autouse fixtures are torn down last): re-read them.
+    sp24.reload_tuning()
     assert sp24.last_kernel_status() == 0, "a kernel raised its bounded-wait timeout flag"
 
 
@@ -145,6 +148,7 @@ def test_decode_known_answer(dt, kernel, bn, m, monkeypatch):
     """B = identity: C must equal the dense A exactly, so every metadata
     nibble, lane and column of the TMEM image is checked."""
     monkeypatch.setenv("SP24_KERNEL", kernel)
+    sp24.reload_tuning()
     k = 256
     n = max(k, bn)
     a = _decode_case(dt, m, k, seed=bn + m)
@@ -180,6 +184,7 @@ def test_alternating_six_pattern(dt, kernel, monkeypatch):
     checked against the oracle with random B."""
     from tests.golden.make_golden import alternating_a
     monkeypatch.setenv("SP24_KERNEL", kernel)
+    sp24.reload_tuning()
     m, n, k = 256, 256, 512
     a = alternating_a(dt, m, k)
     rng = np.random.default_rng(9)
@@ -231,18 +236,10 @@ def test_kernels_agree():
     a, b, *_ = oracle.host_case(gen, 1, m, n, k, False)
     ac_t, e_t = sp24.compress(to_dev(a, 1))
     b_t = to_dev(b, 1)
-    old = os.environ.get("SP24_KERNEL")
-    try:
-        os.environ["SP24_KERNEL"] = "1sm"
-        c1, _ = sp24.gemm(ac_t, e_t, b_t, m, n, k, tile_n=256)
-        os.environ["SP24_KERNEL"] = "2sm"
-        c2, _ = sp24.gemm(ac_t, e_t, b_t, m, n, k)
-        torch.cuda.synchronize()
-    finally:
-        if old is None:
-            os.environ.pop("SP24_KERNEL", None)
-        else:
-            os.environ["SP24_KERNEL"] = old
+    c1, _ = _with_env({"SP24_KERNEL": "1sm"},
+                      lambda: sp24.gemm(ac_t, e_t, b_t, m, n, k, tile_n=256))
+    c2, _ = _with_env({"SP24_KERNEL": "2sm"}, lambda: sp24.gemm(ac_t, e_t, b_t, m, n, k))
+    torch.cuda.synchronize()
     assert (c1 - c2).abs().max().item() <= 1e-5
 
 
@@ -259,16 +256,10 @@ SPLITK_CASES = [
 
 
 def _with_env(env, fn):
-    old = {k: os.environ.get(k) for k in env}
-    os.environ.update(env)
-    try:
+    """Run fn with the SP24_* tuning variables of `env` in effect (the library
+    reads them once, so sp24.tuning_env also makes it re-read them)."""
+    with sp24.tuning_env(env):
         return fn()
-    finally:
-        for k, v in old.items():
-            if v is None:
-                os.environ.pop(k, None)
-            else:
-                os.environ[k] = v
 
 
 NARROW_PAIR_CASES = [
@@ -956,14 +947,10 @@ def test_bounded_wait_timeout_returns_error_and_context_survives():
         status = torch.zeros(1, dtype=torch.int32, device=DEV)
         d = sp24.make_desc(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC, c_f32=c,
                            status=status)
-        os.environ["SP24_KERNEL"] = kernel
-        os.environ["SP24_SPLITS"] = "4"     # the split-K case waits in a cluster of 4
-        try:
-            rc = sp24.load().sp24_selftest_timeout(ctypes.byref(d), 2_000_000,
-                                                   torch.cuda.current_stream().cuda_stream)
-        finally:
-            os.environ.pop("SP24_KERNEL", None)
-            os.environ.pop("SP24_SPLITS", None)
+        # the split-K case waits in a cluster of 4
+        rc = _with_env({"SP24_KERNEL": kernel, "SP24_SPLITS": "4"},
+                       lambda: sp24.load().sp24_selftest_timeout(
+                           ctypes.byref(d), 2_000_000, torch.cuda.current_stream().cuda_stream))
         assert rc == 6
         c2, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC)
         check_c(c2, c_ref, a, b, 1)

@@ -70,3 +70,38 @@ def test_noalloc_rejects_problems_beyond_its_buffer():
     d.a_c, d.meta, d.b, d.c_f32 = 0x10000, 0x20000, 0x30000, 0x40000
     d.meta_format = sp24.META_REF
     assert sp24.load().sp24_gemm_noalloc(ctypes.byref(d), None) == 10
+
+
+def _fake_desc(dt, m, n, k, meta_format, ldb=0):
+    d = sp24.GemmDesc()
+    d.dtype, d.m, d.n, d.k = dt, m, n, k
+    d.a_c, d.meta, d.b, d.c_f32 = 0x10000, 0x20000, 0x30000, 0x40000
+    d.meta_format, d.ldb = meta_format, ldb
+    return d
+
+
+def test_noalloc_counts_padded_b_toward_its_limit():
+    """B whose row pitch breaks the 16-byte rule is staged padded in the same
+    buffer, so its copy counts toward the limit: refused when the padded B
+    alone is too large (tcgen05 metadata, nothing else in the buffer), and
+    when metadata image plus padded B are too large although each would fit
+    alone.  Host-side checks only: nothing is launched."""
+    lib = sp24.load()
+    limit = 16 << 20
+    # 128 x 16384 bf16 A, B 16384 x 1001: padded pitch 1008 elements = 33 MB
+    d = _fake_desc(1, 128, 1001, 16384, sp24.META_TC)
+    assert sp24.workspace_bytes(d) > limit
+    assert lib.sp24_gemm_noalloc(ctypes.byref(d), None) == 10
+    # 4096 x 16384 A: 8.4 MB image; B 16384 x 301 (602 B rows): 9.96 MB padded
+    d = _fake_desc(1, 4096, 301, 16384, sp24.META_REF)
+    assert sp24.meta_tc_bytes(4096, 16384) < limit
+    assert sp24.workspace_bytes(d) - sp24.meta_tc_bytes(4096, 16384) < limit
+    assert sp24.workspace_bytes(d) > limit
+    assert lib.sp24_gemm_noalloc(ctypes.byref(d), None) == 10
+
+
+def test_noalloc_limit_boundary():
+    """The largest documented fit: an 8192 x 16384 A's metadata image is
+    exactly the 16 MiB buffer."""
+    d = _fake_desc(1, 8192, 256, 16384, sp24.META_REF)
+    assert sp24.workspace_bytes(d) == sp24.meta_tc_bytes(8192, 16384) == 16 << 20
