@@ -53,6 +53,8 @@ METRIC = "2:4 GEMM dense-equiv TFLOP/s & % of sparse tensor peak at 1/2/4/8 B200
 PAIRS = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
 
 CONFIGS = {
+    1: dict(name="fp16 2:4 GEMM m64n128k32, one tile (config 1)", dt=0, m=64, n=128, k=32,
+            out=("f32",), dist="normal"),
     2: dict(name="bf16 2:4 GEMM M=N=K=8192, fp32+bf16 out (config 2)", dt=1, m=8192, n=8192,
             k=8192, out=("f32", "bf16"), dist="uniform"),
     3: dict(name="e4m3 2:4 GEMM M=N=K=16384, bf16 out x 1/(sA sB) (config 3)", dt=2, m=16384,
@@ -83,6 +85,22 @@ def config_for(args):
                            " one fused launch, magnitude-pruned N(0,0.02) (config 4)")
             cfg["gemms"] = 2
     return cfg
+
+
+class stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration (native libraries
+    write to the descriptor, not to sys.stdout)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
 
 
 def log(*a):
@@ -234,8 +252,13 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(cfg, rank, torch, sp24, seed_a=1234):
-    """Device-resident A (2:4), its compression + tcgen05 metadata image, B."""
+PARITY_ROWS = 16
+
+
+def make_inputs(cfg, rank, torch, sp24, seed_a=1234, keep_rows=False):
+    """Device-resident A (2:4), its compression + tcgen05 metadata image, B.
+    keep_rows: also return PARITY_ROWS seeded rows of the dense A (as the
+    GEMM sees it: quantised for e4m3) and their indices."""
     dev = torch.device("cuda")
     dt, m, n, k = cfg["dt"], cfg["m"], cfg["n"], cfg["k"]
     g = torch.Generator(device=dev).manual_seed(seed_a)        # A replicated on every rank
@@ -268,11 +291,193 @@ def make_inputs(cfg, rank, torch, sp24, seed_a=1234):
             scale_a, scale_b = sa.item(), sb.item()
         else:
             a, b = a.to(tdt), b.to(tdt)
+    sample = None
+    if keep_rows:
+        import numpy as np
+        rows = np.sort(np.random.default_rng(97).choice(m, min(m, PARITY_ROWS), replace=False))
+        sample = (a[torch.from_numpy(rows).to(dev)].clone(), rows)
     ac, meta = sp24.compress(a)
     del a
     img = sp24.repack_meta(meta, m, k, ac.dtype)
     torch.cuda.synchronize()
+    if keep_rows:
+        return ac, meta, img, b, 1.0 / (scale_a * scale_b), sample
     return ac, meta, img, b, 1.0 / (scale_a * scale_b)
+
+
+def parity_check(torch, dt, sample, b, c32, c16, alpha, k, sample_up=None):
+    """The bench's own output check: the PARITY_ROWS sampled rows of this
+    rank's C against an fp32 product of the same rows computed by torch on
+    the device (TF32 off), as the K-scaled row-norm error
+    max |C - C_ref| / (|A_r| |B_n| alpha / sqrt(K)).  With sample_up (the
+    gated SwiGLU mode) the reference is silu(A_gate B) * (A_up B) and the
+    scale the product of both GEMMs' scales.  Returns (max error, tolerance)."""
+    a_rows, rows = sample
+    prec = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        def f32(t):
+            return t.view(torch.float8_e4m3fn).float() if dt == 2 else t.float()
+        af, bf = f32(a_rows), f32(b)
+        ref = (af @ bf) * alpha
+        denom = torch.outer(af.norm(dim=1), bf.norm(dim=0)) * (alpha / k ** 0.5)
+        if sample_up is not None:
+            uf = f32(sample_up[0])
+            up = uf @ bf
+            ref = torch.nn.functional.silu(ref) * up
+            denom = denom * torch.outer(uf.norm(dim=1), bf.norm(dim=0)) / k ** 0.5
+        idx = torch.from_numpy(rows).to(a_rows.device)
+        got = c32[idx] if c32 is not None else c16[idx].float()
+        err = ((got - ref).abs() / denom.clamp_min(1e-30)).max().item()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prec
+    tol = 2e-2 if (dt == 2 or c32 is None) else 1e-2
+    return err, tol
+
+
+def strong_scaling(args, world, rank, dist, torch, sp24):
+    """Configuration 5 as strong scaling: fp16 M = K = 32768 with its N = 65536
+    columns fixed in total and split over the ranks (sp24_shard_columns,
+    256-column blocks; A replicated, B and C local, no collective on the GEMM
+    path).  Reports the sharded GEMM's time per step (CUDA events, max over
+    ranks), the same whole problem on rank 0 alone (one GPU, B and C of all
+    65536 columns) and t_1 / (world t_world); checks that the sampled rows of
+    every shard equal the one-GPU result bit for bit; then times the fused
+    all-gather separately: each rank's GEMM also stores its columns into
+    every rank's full C over NVLink (sp24_gemm_allgather, CUDA IPC peer
+    pointers), one 1-element all-reduce per step as the completion barrier."""
+    import ctypes
+    lib = sp24.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream()
+    m, k, ntot = 32768, 32768, 65536
+    steps = max(1, args.strong_steps)
+    n0, n1 = sp24.shard_columns(ntot, world, rank, 256)
+    n = n1 - n0
+    cfg = dict(CONFIGS[5], n=n)
+    ac, meta, img, b, alpha, sample = make_inputs(cfg, rank, torch, sp24, keep_rows=True)
+    del meta
+    rows = torch.from_numpy(sample[1]).to(dev)
+    del sample
+    c = torch.empty((m, n), dtype=torch.float32, device=dev)
+    d = sp24.make_desc(ac, img, b, m, n, k, meta_format=sp24.META_TC, c_f32=c, dtype=torch.float16)
+
+    def timed(desc, reps, peers=None, tick=None):
+        for _ in range(2 if reps > 1 else 1):
+            rc = (lib.sp24_gemm_allgather(ctypes.byref(desc), ctypes.byref(peers), stream.cuda_stream)
+                  if peers is not None else lib.sp24_gemm(ctypes.byref(desc), stream.cuda_stream))
+            if rc != 0:
+                raise sp24.Sp24Error(rc, "strong scaling GEMM")
+            if tick is not None:
+                dist.all_reduce(tick)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            rc = (lib.sp24_gemm_allgather(ctypes.byref(desc), ctypes.byref(peers), stream.cuda_stream)
+                  if peers is not None else lib.sp24_gemm(ctypes.byref(desc), stream.cuda_stream))
+            if rc != 0:
+                raise sp24.Sp24Error(rc, "strong scaling GEMM")
+            if tick is not None:
+                dist.all_reduce(tick)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    # The sharded GEMM.
+    t = torch.tensor([timed(d, steps)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_n = t.item()
+    mine = c[rows].contiguous()
+    shards = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(shards, mine)
+
+    # The whole problem on rank 0 alone (the others wait at the barrier).
+    t1, equal = 0.0, 1
+    if rank == 0:
+        parts = []
+        for r in range(world):
+            r0, r1 = sp24.shard_columns(ntot, world, r, 256)
+            gb = torch.Generator(device=dev).manual_seed(4321 + r)
+            parts.append(torch.randn((k, r1 - r0), device=dev, generator=gb).to(torch.float16))
+        bfull = torch.cat(parts, dim=1)
+        del parts
+        cfull = torch.empty((m, ntot), dtype=torch.float32, device=dev)
+        dfull = sp24.make_desc(ac, img, bfull, m, ntot, k, meta_format=sp24.META_TC, c_f32=cfull,
+                               dtype=torch.float16)
+        for _ in range(1):
+            lib.sp24_gemm(ctypes.byref(dfull), stream.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            lib.sp24_gemm(ctypes.byref(dfull), stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t1 = e0.elapsed_time(e1) / steps
+        got = cfull[rows]
+        for r in range(world):
+            r0, r1 = sp24.shard_columns(ntot, world, r, 256)
+            if not torch.equal(got[:, r0:r1], shards[r]):
+                equal = 0
+        del bfull, cfull, got
+        torch.cuda.empty_cache()
+    dist.barrier()
+
+    # Fused all-gather into every rank's full C (timed separately).
+    full = torch.empty((m, ntot), dtype=torch.float32, device=dev)
+    handle = sp24.ipc_handle(full)
+    handles = [None] * world
+    dist.all_gather_object(handles, handle)
+    opened, peers = {}, []
+    for r in range(world):
+        if r == rank:
+            continue
+        h, off = handles[r]
+        if h not in opened:
+            opened[h] = sp24.ipc_open(h)
+        peers.append(opened[h] + off + n0 * 4)
+    po = sp24.PeerOut()
+    po.n_peers = len(peers)
+    for i, addr in enumerate(peers):
+        po.c_f32[i] = addr
+    dg = sp24.make_desc(ac, img, b, m, n, k, meta_format=sp24.META_TC, c_f32=full[:, n0:n1],
+                        dtype=torch.float16)
+    tick = torch.zeros(1, device=dev)
+    tg = torch.tensor([timed(dg, steps, peers=po, tick=tick)], device=dev)
+    dist.all_reduce(tg, op=dist.ReduceOp.MAX)
+    got = full[rows]
+    ok = all(torch.equal(got[:, sp24.shard_columns(ntot, world, r, 256)[0]:
+                             sp24.shard_columns(ntot, world, r, 256)[1]], shards[r])
+             for r in range(world))
+    flag = torch.tensor([1 if ok else 0, equal], device=dev, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.barrier()
+    for base in opened.values():
+        sp24.ipc_close(base)
+    del full, c, ac, img, b, got
+    torch.cuda.empty_cache()
+    flops = 2.0 * m * ntot * k
+    t1 = torch.tensor([t1], device=dev)
+    dist.all_reduce(t1, op=dist.ReduceOp.MAX)
+    t1 = t1.item()
+    sent = m * n * 4 * (world - 1)
+    return {"workload": "fp16 2:4 GEMM M=K=32768, N=65536 in total split over the ranks "
+                        "(config 5), fp32 out",
+            "n_total": ntot, "n_per_rank": n, "steps": steps,
+            "ms_per_step": t_n, "tflops": flops / (t_n * 1e-3) / 1e12,
+            "one_gpu_ms_per_step": t1, "one_gpu_tflops": flops / (t1 * 1e-3) / 1e12,
+            "speedup": t1 / t_n, "efficiency": t1 / (world * t_n),
+            "shards_bit_equal_to_one_gpu": bool(flag[1].item()),
+            "fused_allgather": {"ms_per_step": tg.item(), "bytes_sent_per_rank": sent,
+                                "ms_beyond_gemm": tg.item() - t_n,
+                                "GB_per_s_per_rank_beyond_gemm":
+                                    sent / (max(tg.item() - t_n, 1e-6) * 1e-3) / 1e9,
+                                "gathered_bit_equal": bool(flag[0].item()),
+                                "what": "GEMM + peer stores of C into every rank's full C + "
+                                        "1-element all-reduce, per step"},
+            "timing": "CUDA events on each rank's stream, max over ranks; one-GPU time on rank 0"}
 
 
 def cpu_reference_rate(cfg, seconds=10.0, threads=None):
@@ -455,6 +660,10 @@ def main():
                          "shards + column permute; fused = sp24_gemm_allgather (peer stores "
                          "over NVLink inside the GEMM)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="N > 1: skip the strong-scaling record (configuration 5 split over "
+                         "the ranks)")
+    ap.add_argument("--strong-steps", type=int, default=5)
     ap.add_argument("--no-probe", action="store_true",
                     help="skip the tensor-pipe probe (roofline peak = 2 x measured dense)")
     ap.add_argument("--ref-seconds", type=float, default=10.0)
@@ -491,13 +700,18 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its version banner on the process's stdout while the
+        # communicator is created; keep stdout for the one JSON line.
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
     if sp24.load().sp24_check_device(local) != 0:
         raise SystemExit("sp24: device is not sm_100 — the library has no other code path")
 
     m, n, k, dt = cfg["m"], cfg["n"], cfg["k"], cfg["dt"]
-    ac, meta, img, b, alpha = make_inputs(cfg, rank, torch, sp24)
+    ac, meta, img, b, alpha, sample = make_inputs(cfg, rank, torch, sp24, keep_rows=True)
     dev = ac.device
     c32 = torch.empty((m, n), dtype=torch.float32, device=dev) if "f32" in cfg["out"] else None
     c16 = torch.empty((m, n), dtype=torch.bfloat16, device=dev) if "bf16" in cfg["out"] else None
@@ -513,7 +727,8 @@ def main():
     if gemms == 2:
         # Second weight (W_up) of the SwiGLU; W_gate is `ac`.
         cfg_up = dict(cfg)
-        ac_up, _, img_up, _, _ = make_inputs(cfg_up, rank, torch, sp24, seed_a=4242)
+        ac_up, _, img_up, _, _, sample_up = make_inputs(cfg_up, rank, torch, sp24, seed_a=4242,
+                                                        keep_rows=True)
         epi = sp24.Epilogue()
         epi.act = sp24.ACT_SILU
         epi.a_c_up, epi.lda_c_up = ac_up.data_ptr(), ac_up.stride(0)
@@ -540,6 +755,8 @@ def main():
     flush_l2 = fits_l2 and args.l2 == "clean"
     weight_bytes = gemms * (m * k // 2 * esz + m * k // 8)
     copies = (2 * L2_BYTES) // weight_bytes + 2 if (fits_l2 and not flush_l2) else 1
+    if args.config == 1:
+        copies = 1      # one tile: latency-bound, timed back to back and per launch below
     descs, epis, keep = [desc], [epi if gemms == 2 else None], []
     for _ in range(1, copies):
         ac_i, img_i = ac.clone(), img.clone()
@@ -650,6 +867,31 @@ def main():
     value = flops_rank * world / (ms_step * 1e-3) / 1e12
     kernel_tflops = flops_rank / (ms_local / args.steps * 1e-3) / 1e12
 
+    # The bench's own correctness evidence, taken on the timed steps' output
+    # before anything else writes C: sampled rows of every rank's C against
+    # torch fp32 on the device (the max over ranks is reported below).
+    perr, ptol = parity_check(torch, dt, sample, b, c32, c16, alpha, k,
+                              sample_up if gemms == 2 else None)
+
+    # Configuration 1 (one 64 x 128 x 32 tile) is latency-bound: besides the
+    # back-to-back rate above, time single launches each between their own
+    # pair of events (launch latency included) and report microseconds.
+    latency = None
+    if args.config == 1:
+        lat = []
+        for _ in range(max(20, min(args.steps, 200))):
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            step()
+            a1.record(stream)
+            a1.synchronize()
+            lat.append(a0.elapsed_time(a1) * 1e3)
+        latency = {"back_to_back_us": ms_step * 1e3, "single_launch_median_us": statistics.median(lat),
+                   "single_launch_min_us": min(lat), "launches": len(lat),
+                   "how": "CUDA events on the launching stream; back to back: the timed steps "
+                          "above; single: one launch between its own events, synchronised"}
+
     # Gated mode: the same SwiGLU as two GEMMs plus torch's silu * mul, timed
     # the same way, for comparison.
     unfused = None
@@ -715,6 +957,19 @@ def main():
 
     # Optional replicated output: all-gather of the C shards over NVLink,
     # timed separately from the GEMM (config 5 option).
+    def gathered_equal(full_t):
+        """Every rank's gathered copy holds, bit for bit, every rank's own
+        GEMM output on the sampled rows (MIN over ranks)."""
+        idx = torch.from_numpy(sample[1]).to(dev)
+        mine = c32[idx].contiguous()
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        rows_full = full_t[idx]
+        ok = all(torch.equal(rows_full[:, r * n:(r + 1) * n], allr[r]) for r in range(world))
+        flag = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        return bool(flag.item())
+
     allgather = None
     if args.allgather in ("nccl", "both") and world > 1 and c32 is not None:
         flat = c32.reshape(-1)
@@ -742,7 +997,8 @@ def main():
         recv = flat.numel() * 4 * (world - 1)
         allgather = {"ms": ta[0].item() + ta[1].item(), "nccl_ms": ta[0].item(),
                      "unshard_ms": ta[1].item(), "bytes_received_per_rank": recv,
-                     "nccl_GB_per_s_per_rank": recv / (ta[0].item() * 1e-3) / 1e9}
+                     "nccl_GB_per_s_per_rank": recv / (ta[0].item() * 1e-3) / 1e9,
+                     "gathered_bit_equal": gathered_equal(full)}
         del out, full
 
     # Fused alternative: every rank's GEMM stores its shard into all ranks'
@@ -796,7 +1052,8 @@ def main():
                     "bytes_sent_per_rank": sent,
                     "tflops": flops_rank * world / (tf_.item() * 1e-3) / 1e12,
                     "what": "sp24_gemm_allgather (GEMM + peer stores of C over NVLink) + "
-                            "1-element all-reduce barrier, per step"}
+                            "1-element all-reduce barrier, per step",
+                    "gathered_bit_equal": gathered_equal(full)}
         barrier()
         for base in opened.values():
             sp24.ipc_close(base)
@@ -920,6 +1177,22 @@ def main():
                "steps": args.e2e_steps, "gpu_launches_per_step": 2,
                "pipeline": "two buffer sets; step i's D2H overlaps step i+1's H2D"}
 
+    if world > 1:
+        pe = torch.tensor([perr], device=dev)
+        dist.all_reduce(pe, op=dist.ReduceOp.MAX)
+        perr = pe.item()
+    parity = {"rows": len(sample[1]), "per_rank": True, "max_row_norm_err": perr, "tol": ptol,
+              "ok": perr <= ptol,
+              "reference": "torch fp32 matmul of the same rows on the device (TF32 off)"}
+    if allgather is not None:
+        parity["nccl_gathered_bit_equal"] = allgather["gathered_bit_equal"]
+    if fused_ag is not None:
+        parity["fused_gathered_bit_equal"] = fused_ag["gathered_bit_equal"]
+
+    strong = None
+    if world > 1 and not args.no_strong:
+        strong = strong_scaling(args, world, rank, dist, torch, sp24)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, kind, cores, sample = cpu_reference_rate(cfg, seconds=args.ref_seconds)
@@ -932,7 +1205,7 @@ def main():
         alg_bytes = in_bytes + out_bytes
         ms_kernel = ms_local / args.steps
         hbm_bound = args.config == 4 and n <= 128
-        tag = {2: "sp24_gemm2sm_bf16_8192", 3: "sp24_gemm2sm_e4m3_16384",
+        tag = {1: "sp24_gemm_config1", 2: "sp24_gemm2sm_bf16_8192", 3: "sp24_gemm2sm_e4m3_16384",
                4: f"sp24_gemm_mlp_{args.layer}_T{n}" + ("_gated" if gemms == 2 else ""),
                5: "sp24_gemm2sm_f16_32768"}[args.config]
         if hbm_bound:
@@ -981,6 +1254,11 @@ def main():
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
+        line["parity"] = parity
+        if latency:
+            line["latency"] = latency
+        if strong:
+            line["strong"] = strong
         if allgather:
             line["allgather"] = allgather
         if fused_ag:

@@ -289,6 +289,63 @@ sp24_status sp24_ipc_get_handle(const void* dev_ptr, void* handle64, size_t* off
 sp24_status sp24_ipc_open_handle(const void* handle64, void** base);
 sp24_status sp24_ipc_close(void* base);
 
+/* One N-sharded GEMM over several GPUs of this process, from one host
+   thread (no reference counterpart: the reference runs on one GPU; the
+   multi-GPU layout is the one its large GEMMs shard along N).  Device g of
+   md->devices owns the columns [n0, n1) = sp24_shard_columns(n, ngpu, g,
+   256) of C; A_c and the metadata are replicated (md->a_c[g], md->meta[g]:
+   the same contents on every device, e.g. through sp24_replicate), B and C
+   are local.  Each device's GEMM is enqueued on md->streams[g] (NULL: that
+   device's legacy default stream); the call returns once every launch is
+   enqueued and restores the caller's current device.
+     md->gemm       the whole problem: dtype, m, n (all columns), k, lda_c,
+                    meta_format, ldb / ldc (see the layouts), alpha, tile_n.
+                    Its pointer, workspace and status fields are ignored.
+     b_layout       SP24_MULTI_FULL: md->b[g] is all of B (k x n, row stride
+                    ldb, 0 = n); SP24_MULTI_SHARD: md->b[g] is device g's
+                    column block alone (k x (n1 - n0), row stride n1 - n0).
+     c_layout       the same for md->c_f32[g] / md->c_bf16[g] (row stride
+                    ldc, 0 = n, for FULL): a FULL C receives device g's
+                    columns, and with allgather_c every device's columns.
+     workspace[g]   device g's workspace (META_REF repack, B padding), at
+                    least sp24_gemm_multi_workspace_bytes(md) bytes, or NULL
+                    when that is 0.
+   allgather_c (FULL C only): every device's epilogue also stores its tiles
+   into the other devices' C over NVLink (peer access is enabled on first
+   use), and each stream is made to wait for every device's launch, so work
+   enqueued on md->streams[g] after this call sees the complete C.  The
+   kernels never wait on a peer.  All structural checks (ngpu 1 ..
+   SP24_MAX_GPUS, distinct devices, layouts, pointers) happen before anything
+   is enqueued. */
+#define SP24_MAX_GPUS 8
+typedef enum sp24_multi_layout { SP24_MULTI_FULL = 0, SP24_MULTI_SHARD = 1 } sp24_multi_layout;
+typedef struct sp24_multi_desc {
+  sp24_gemm_desc gemm;
+  int ngpu;
+  int devices[SP24_MAX_GPUS];
+  sp24_stream_t streams[SP24_MAX_GPUS];
+  const void* a_c[SP24_MAX_GPUS];
+  const uint8_t* meta[SP24_MAX_GPUS];
+  const void* b[SP24_MAX_GPUS];
+  sp24_multi_layout b_layout;
+  float* c_f32[SP24_MAX_GPUS];
+  void* c_bf16[SP24_MAX_GPUS];
+  sp24_multi_layout c_layout;
+  void* workspace[SP24_MAX_GPUS];
+  size_t workspace_bytes;
+} sp24_multi_desc;
+sp24_status sp24_gemm_multi(const sp24_multi_desc* md, int allgather_c);
+/* Workspace each device needs for sp24_gemm_multi(md, ...): the largest of
+   the per-device column-block GEMMs' needs (0 if none, or if md is invalid). */
+size_t sp24_gemm_multi_workspace_bytes(const sp24_multi_desc* md);
+
+/* Replication helper for sp24_gemm_multi's A_c / metadata: copies `bytes`
+   from src (on device src_device) to dst[g] on each devices[g] (peer copies
+   over NVLink, enqueued on streams[g]; a destination equal to src is
+   skipped).  No reference counterpart. */
+sp24_status sp24_replicate(const void* src, int src_device, size_t bytes, int ngpu,
+                           const int* devices, void* const* dst, const sp24_stream_t* streams);
+
 /* Multi-GPU N-sharding helpers (no collective on the GEMM path).
    Columns [n0, n1) of C belong to `rank` of `world`; boundaries are multiples
    of `align` (the tile width) except the last. */

@@ -401,6 +401,7 @@ sp24::PairParams pair_params(const Prepared& p, int bkd, int tile_m, int tile_n)
   // itself.  SP24_C_EVICT=0 turns it off.
   P.c_evict_first =
       (p.tune.c_evict && p.peers.n == 0 && !p.gate_from_c && !p.c_reread) ? 1 : 0;
+  P.static_weights = p.static_weights;
   P.status = p.status;
   P.timeout_ns = p.timeout_ns;
   P.stall_producer = p.stall_producer;
@@ -1146,6 +1147,207 @@ sp24_status sp24_gemm_allgather(const sp24_gemm_desc* d, const sp24_peer_out* pe
                                 sp24_stream_t stream) {
   if (peers == nullptr) return SP24_ERR_ARG;
   return gemm_impl(d, as_stream(stream), kDefaultTimeoutNs, 0, nullptr, peers);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Peer access between devices of this process, enabled once per ordered
+// pair (sp24_gemm_multi's fused all-gather stores into peers' C).
+std::mutex g_peer_mu;
+bool g_peer_on[kMaxDevices][kMaxDevices];
+
+sp24_status enable_peer(int dev, int peer) {
+  std::lock_guard<std::mutex> lk(g_peer_mu);
+  if (g_peer_on[dev][peer]) return SP24_OK;
+  int can = 0;
+  SP24_CUDA_TRY(cudaDeviceCanAccessPeer(&can, dev, peer));
+  if (!can) return SP24_ERR_CUDA;
+  SP24_CUDA_TRY(cudaSetDevice(dev));
+  const cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    return SP24_ERR_CUDA;
+  }
+  (void)cudaGetLastError();
+  g_peer_on[dev][peer] = true;
+  return SP24_OK;
+}
+
+// Restores the calling thread's current device when it leaves scope.
+struct DeviceRestore {
+  int dev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      dev = -1;
+    }
+  }
+  ~DeviceRestore() {
+    if (dev >= 0) (void)cudaSetDevice(dev);
+  }
+};
+
+// Host-side checks of a multi-GPU descriptor (no CUDA calls).
+sp24_status validate_multi(const sp24_multi_desc* md, int allgather_c) {
+  if (md == nullptr) return SP24_ERR_ARG;
+  const int ng = md->ngpu;
+  if (ng < 1 || ng > SP24_MAX_GPUS) return SP24_ERR_ARG;
+  if ((md->b_layout != SP24_MULTI_FULL && md->b_layout != SP24_MULTI_SHARD) ||
+      (md->c_layout != SP24_MULTI_FULL && md->c_layout != SP24_MULTI_SHARD))
+    return SP24_ERR_ARG;
+  if (allgather_c && md->c_layout != SP24_MULTI_FULL) return SP24_ERR_ARG;
+  const bool want32 = md->c_f32[0] != nullptr, want16 = md->c_bf16[0] != nullptr;
+  if (!want32 && !want16) return SP24_ERR_ARG;
+  for (int g = 0; g < ng; ++g) {
+    if (md->devices[g] < 0 || md->devices[g] >= kMaxDevices) return SP24_ERR_ARG;
+    for (int h = 0; h < g; ++h)
+      if (md->devices[h] == md->devices[g]) return SP24_ERR_ARG;
+    if (md->a_c[g] == nullptr || md->meta[g] == nullptr || md->b[g] == nullptr) return SP24_ERR_ARG;
+    if ((md->c_f32[g] != nullptr) != want32 || (md->c_bf16[g] != nullptr) != want16)
+      return SP24_ERR_ARG;
+  }
+  if (md->gemm.m <= 0 || md->gemm.n <= 0 || md->gemm.k <= 0) return SP24_ERR_SHAPE;
+  return SP24_OK;
+}
+
+// Device g's share of a multi-GPU GEMM as a one-device descriptor; sets
+// *empty when the device owns no columns.
+sp24_gemm_desc shard_desc(const sp24_multi_desc* md, int g, int* n0_out, bool* empty) {
+  const sp24_gemm_desc& G = md->gemm;
+  int n0 = 0, n1 = 0;
+  sp24_shard_columns(G.n, md->ngpu, g, 256, &n0, &n1);
+  *n0_out = n0;
+  *empty = n1 <= n0;
+  const size_t es = static_cast<size_t>(esize(G.dtype));
+  sp24_gemm_desc d = G;
+  d.n = std::max(1, n1 - n0);
+  d.a_c = md->a_c[g];
+  d.meta = md->meta[g];
+  if (md->b_layout == SP24_MULTI_FULL) {
+    d.b = static_cast<const uint8_t*>(md->b[g]) + static_cast<size_t>(n0) * es;
+    d.ldb = G.ldb ? G.ldb : G.n;
+  } else {
+    d.b = md->b[g];
+    d.ldb = n1 - n0;
+  }
+  if (md->c_layout == SP24_MULTI_FULL) {
+    d.c_f32 = md->c_f32[g] != nullptr ? md->c_f32[g] + n0 : nullptr;
+    d.c_bf16 = md->c_bf16[g] != nullptr ? static_cast<uint8_t*>(md->c_bf16[g]) + 2 * static_cast<size_t>(n0)
+                                        : nullptr;
+    d.ldc = G.ldc ? G.ldc : G.n;
+  } else {
+    d.c_f32 = md->c_f32[g];
+    d.c_bf16 = md->c_bf16[g];
+    d.ldc = n1 - n0;
+  }
+  d.workspace = md->workspace[g];
+  d.workspace_bytes = md->workspace_bytes;
+  d.status_dev = nullptr;
+  return d;
+}
+
+}  // namespace
+
+extern "C" {
+
+sp24_status sp24_gemm_multi(const sp24_multi_desc* md, int allgather_c) {
+  sp24_status st = validate_multi(md, allgather_c);
+  if (st != SP24_OK) return st;
+  const int ng = md->ngpu;
+  sp24_gemm_desc d[SP24_MAX_GPUS];
+  int n0[SP24_MAX_GPUS];
+  bool empty[SP24_MAX_GPUS];
+  for (int g = 0; g < ng; ++g) {
+    d[g] = shard_desc(md, g, &n0[g], &empty[g]);
+    if (!empty[g]) {
+      st = validate(&d[g]);
+      if (st != SP24_OK) return st;
+    }
+  }
+  DeviceRestore restore;
+  if (allgather_c && ng > 1)
+    for (int g = 0; g < ng; ++g)
+      for (int h = 0; h < ng; ++h)
+        if (h != g) {
+          st = enable_peer(md->devices[g], md->devices[h]);
+          if (st != SP24_OK) return st;
+        }
+  for (int g = 0; g < ng; ++g) {
+    if (empty[g]) continue;
+    SP24_CUDA_TRY(cudaSetDevice(md->devices[g]));
+    const cudaStream_t s = as_stream(md->streams[g]);
+    if (allgather_c && ng > 1) {
+      sp24_peer_out po{};
+      for (int h = 0; h < ng; ++h) {
+        if (h == g) continue;
+        po.c_f32[po.n_peers] = md->c_f32[h] != nullptr ? md->c_f32[h] + n0[g] : nullptr;
+        po.c_bf16[po.n_peers] = md->c_bf16[h] != nullptr
+                                    ? static_cast<uint8_t*>(md->c_bf16[h]) + 2 * static_cast<size_t>(n0[g])
+                                    : nullptr;
+        ++po.n_peers;
+      }
+      st = gemm_impl(&d[g], s, kDefaultTimeoutNs, 0, nullptr, &po);
+    } else {
+      st = gemm_impl(&d[g], s, kDefaultTimeoutNs, 0);
+    }
+    if (st != SP24_OK) return st;
+  }
+  if (allgather_c && ng > 1) {
+    // Every stream waits for every device's launch: the gathered C is
+    // complete for work enqueued after this call.  Events are per call (no
+    // state shared between concurrent callers) and released at once; the
+    // waits already enqueued keep what they need.
+    cudaEvent_t ev[SP24_MAX_GPUS] = {};
+    for (int g = 0; g < ng; ++g) {
+      SP24_CUDA_TRY(cudaSetDevice(md->devices[g]));
+      SP24_CUDA_TRY(cudaEventCreateWithFlags(&ev[g], cudaEventDisableTiming));
+      SP24_CUDA_TRY(cudaEventRecord(ev[g], as_stream(md->streams[g])));
+    }
+    sp24_status wst = SP24_OK;
+    for (int g = 0; g < ng && wst == SP24_OK; ++g) {
+      if (cudaSetDevice(md->devices[g]) != cudaSuccess) wst = SP24_ERR_CUDA;
+      for (int h = 0; h < ng && wst == SP24_OK; ++h)
+        if (h != g && cudaStreamWaitEvent(as_stream(md->streams[g]), ev[h], 0) != cudaSuccess)
+          wst = SP24_ERR_CUDA;
+    }
+    for (int g = 0; g < ng; ++g) {
+      (void)cudaSetDevice(md->devices[g]);
+      (void)cudaEventDestroy(ev[g]);
+    }
+    if (wst != SP24_OK) (void)cudaGetLastError();
+    return wst;
+  }
+  return SP24_OK;
+}
+
+size_t sp24_gemm_multi_workspace_bytes(const sp24_multi_desc* md) {
+  if (validate_multi(md, 0) != SP24_OK) return 0;
+  size_t need = 0;
+  for (int g = 0; g < md->ngpu; ++g) {
+    int n0 = 0;
+    bool empty = false;
+    const sp24_gemm_desc d = shard_desc(md, g, &n0, &empty);
+    if (!empty && validate(&d) == SP24_OK) need = std::max(need, plan_workspace(&d).total);
+  }
+  return need;
+}
+
+sp24_status sp24_replicate(const void* src, int src_device, size_t bytes, int ngpu,
+                           const int* devices, void* const* dst, const sp24_stream_t* streams) {
+  if (src == nullptr || devices == nullptr || dst == nullptr || ngpu < 1 || ngpu > SP24_MAX_GPUS)
+    return SP24_ERR_ARG;
+  for (int g = 0; g < ngpu; ++g)
+    if (dst[g] == nullptr || devices[g] < 0) return SP24_ERR_ARG;
+  DeviceRestore restore;
+  for (int g = 0; g < ngpu; ++g) {
+    if (dst[g] == src && devices[g] == src_device) continue;
+    SP24_CUDA_TRY(cudaSetDevice(devices[g]));
+    SP24_CUDA_TRY(cudaMemcpyPeerAsync(dst[g], devices[g], src, src_device, bytes,
+                                      as_stream(streams != nullptr ? streams[g] : nullptr)));
+  }
+  return SP24_OK;
 }
 
 sp24_status sp24_ipc_get_handle(const void* dev_ptr, void* handle64, size_t* offset) {

@@ -72,6 +72,8 @@ struct PairParams {
   int vec_f32;   // 2: 32-byte stores, 1: 16-byte, 0: scalar
   int vec_bf16;
   int c_evict_first;  // 32-byte C stores under an L2 evict-first policy (no peers)
+  int static_weights; // A_c / metadata not written by in-flight work: their producer warp
+                      // starts before the previous kernel of the stream completes
   int* status;
   unsigned long long timeout_ns;
   int stall_producer;
@@ -489,7 +491,10 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
   griddep_launch_dependents();
 
   if (warp == 0 || warp == kPairBWarp) {
-    griddep_wait();   // inputs may come from the previous kernel in the stream
+    // Inputs may come from the previous kernel in the stream.  Under the
+    // static-weights hint the A_c / metadata warp starts at once: only B (and,
+    // through the mbarrier chain, every C store) waits for that kernel.
+    if (warp == kPairBWarp || !P.static_weights) griddep_wait();
     // ------------------------------------------------------------ producers
     // Two warps load each stage: warp 0 the A_c box (lane 0) and the metadata
     // atoms (lanes 1..E_PER), warp 10 the B boxes (one per lane).  Splitting

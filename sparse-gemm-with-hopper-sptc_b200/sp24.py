@@ -41,6 +41,7 @@ EXPORTS = [
     "sp24_gemm_noalloc", "sp24_quantize_e5m2", "sp24_gemm_fused", "sp24_repack_meta_k16",
     "sp24_gemm_allgather", "sp24_ipc_get_handle", "sp24_ipc_open_handle", "sp24_ipc_close",
     "sp24_set_launch_hints", "sp24_get_launch_hints", "sp24_reload_tuning",
+    "sp24_gemm_multi", "sp24_replicate", "sp24_gemm_multi_workspace_bytes",
 ]
 MAX_PEERS = 7
 HINT_NONE, HINT_STATIC_WEIGHTS = 0, 1
@@ -79,6 +80,20 @@ class PeerOut(Structure):
     _fields_ = [("n_peers", c_int), ("c_f32", c_void_p * 7), ("c_bf16", c_void_p * 7)]
 
 
+MAX_GPUS = 8
+MULTI_FULL, MULTI_SHARD = 0, 1
+
+
+class MultiDesc(Structure):
+    _fields_ = [
+        ("gemm", GemmDesc), ("ngpu", c_int), ("devices", c_int * MAX_GPUS),
+        ("streams", c_void_p * MAX_GPUS), ("a_c", c_void_p * MAX_GPUS),
+        ("meta", c_void_p * MAX_GPUS), ("b", c_void_p * MAX_GPUS), ("b_layout", c_int),
+        ("c_f32", c_void_p * MAX_GPUS), ("c_bf16", c_void_p * MAX_GPUS), ("c_layout", c_int),
+        ("workspace", c_void_p * MAX_GPUS), ("workspace_bytes", c_size_t),
+    ]
+
+
 _lib = None
 
 
@@ -102,6 +117,11 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_gemm_noalloc.argtypes = [POINTER(GemmDesc), c_void_p]
     lib.sp24_gemm_fused.argtypes = [POINTER(GemmDesc), POINTER(Epilogue), c_void_p]
     lib.sp24_gemm_allgather.argtypes = [POINTER(GemmDesc), POINTER(PeerOut), c_void_p]
+    lib.sp24_gemm_multi.argtypes = [POINTER(MultiDesc), c_int]
+    lib.sp24_gemm_multi_workspace_bytes.argtypes = [POINTER(MultiDesc)]
+    lib.sp24_gemm_multi_workspace_bytes.restype = c_size_t
+    lib.sp24_replicate.argtypes = [c_void_p, c_int, c_size_t, c_int, POINTER(c_int),
+                                   POINTER(c_void_p), POINTER(c_void_p)]
     lib.sp24_ipc_get_handle.argtypes = [c_void_p, c_void_p, POINTER(c_size_t)]
     lib.sp24_ipc_open_handle.argtypes = [c_void_p, POINTER(c_void_p)]
     lib.sp24_ipc_close.argtypes = [c_void_p]
@@ -129,6 +149,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.sp24_unshard_columns_f32.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                              c_void_p]
     for name in ("sp24_gemm", "sp24_gemm_noalloc", "sp24_gemm_fused", "sp24_gemm_allgather",
+                 "sp24_gemm_multi", "sp24_replicate",
                  "sp24_ipc_get_handle", "sp24_ipc_open_handle", "sp24_ipc_close",
                  "sp24_selftest_timeout",
                  "sp24_last_kernel_status",
@@ -333,6 +354,65 @@ def gemm_allgather(desc: GemmDesc, peer_f32=(), peer_bf16=(), stream=None) -> No
         po.c_bf16[i] = a
     _check(load().sp24_gemm_allgather(ctypes.byref(desc), ctypes.byref(po), _stream(stream)),
            "sp24_gemm_allgather")
+
+
+def replicate(src, dsts, streams=None) -> None:
+    """sp24_replicate: copy tensor src into each tensor of dsts (one per
+    device, same size), enqueued on each destination device's stream."""
+    n = len(dsts)
+    devs = (c_int * n)(*[t.device.index for t in dsts])
+    ptrs = (c_void_p * n)(*[t.data_ptr() for t in dsts])
+    strs = (c_void_p * n)(*[(s.cuda_stream if s is not None else None) for s in
+                            (streams or [None] * n)])
+    _check(load().sp24_replicate(src.data_ptr(), src.device.index,
+                                 src.numel() * src.element_size(), n, devs, ptrs, strs),
+           "sp24_replicate")
+
+
+def make_multi_desc(m, n, k, dtype, a_c, meta, b, *, c_f32=None, c_bf16=None,
+                    meta_format=META_TC, b_layout=MULTI_FULL, c_layout=MULTI_FULL, ldb=0, ldc=0,
+                    alpha=1.0, workspaces=None, streams=None) -> MultiDesc:
+    """A sp24_multi_desc from per-device tensors (lists, one per GPU, in
+    device order)."""
+    md = MultiDesc()
+    g = md.gemm
+    g.dtype, g.m, g.n, g.k = dtype_code(dtype), m, n, k
+    g.meta_format, g.ldb, g.ldc, g.alpha = meta_format, ldb, ldc, alpha
+    md.ngpu = len(a_c)
+    for i, t in enumerate(a_c):
+        md.devices[i] = t.device.index
+        md.a_c[i], md.meta[i], md.b[i] = t.data_ptr(), meta[i].data_ptr(), b[i].data_ptr()
+        md.c_f32[i] = _ptr(c_f32[i]) if c_f32 is not None else None
+        md.c_bf16[i] = _ptr(c_bf16[i]) if c_bf16 is not None else None
+        md.streams[i] = streams[i].cuda_stream if streams is not None else None
+        if workspaces is not None and workspaces[i] is not None:
+            md.workspace[i] = workspaces[i].data_ptr()
+    if workspaces is not None:
+        md.workspace_bytes = min(w.numel() for w in workspaces if w is not None)
+    md.b_layout, md.c_layout = b_layout, c_layout
+    g.lda_c = a_c[0].stride(0)
+    return md
+
+
+def multi_workspace_bytes(md: MultiDesc) -> int:
+    return int(load().sp24_gemm_multi_workspace_bytes(ctypes.byref(md)))
+
+
+def gemm_multi(md: MultiDesc, allgather_c: bool = False) -> list:
+    """sp24_gemm_multi; when md carries no workspaces and the problem needs
+    them, allocates one per device first.  Returns the workspaces (keep them
+    alive until the streams are done)."""
+    import torch
+    keep = []
+    need = multi_workspace_bytes(md)
+    if need and not any(md.workspace[i] for i in range(md.ngpu)):
+        for i in range(md.ngpu):
+            w = torch.empty(need, dtype=torch.uint8, device=torch.device("cuda", md.devices[i]))
+            md.workspace[i] = w.data_ptr()
+            keep.append(w)
+        md.workspace_bytes = need
+    _check(load().sp24_gemm_multi(ctypes.byref(md), 1 if allgather_c else 0), "sp24_gemm_multi")
+    return keep
 
 
 def set_launch_hints(hints: int) -> None:

@@ -115,3 +115,47 @@ def test_compress_and_prune_argument_checks():
     assert lib.sp24_compress(0, 0x1008, 8, 16, 0, 0x2000, 0, 0x3000, 0x4000, None, None) == 2
     assert lib.sp24_prune_2of4(0, 0x1000, 8, 6, 0, 0x2000, 0, None) == 1
     assert lib.sp24_repack_meta(0, 0x1000, 64, 48, 0x2000, None) == 1
+
+
+def _multi(**kw):
+    md = sp24.MultiDesc()
+    md.gemm.dtype, md.gemm.m, md.gemm.n, md.gemm.k = 1, 256, 512, 256
+    md.gemm.meta_format = sp24.META_TC
+    md.ngpu = kw.pop("ngpu", 2)
+    for g in range(min(md.ngpu, sp24.MAX_GPUS)):
+        md.devices[g] = g
+        md.a_c[g], md.meta[g], md.b[g] = 0x10000, 0x20000, 0x30000
+        md.c_f32[g] = 0x40000
+    for k, v in kw.items():
+        setattr(md, k, v)
+    return md
+
+
+def test_gemm_multi_rejects_bad_descriptors_before_any_launch():
+    """sp24_gemm_multi's structural checks run on the host before any CUDA
+    call: GPU count, repeated devices, layouts, missing pointers, and an
+    all-gather into column-block (SHARD) outputs."""
+    lib = sp24.load()
+    call = lambda md, ag=0: lib.sp24_gemm_multi(ctypes.byref(md), ag)
+    assert call(_multi(ngpu=0)) == 8
+    assert call(_multi(ngpu=9)) == 8
+    md = _multi()
+    md.devices[1] = 0
+    assert call(md) == 8
+    md = _multi()
+    md.b[1] = None
+    assert call(md) == 8
+    md = _multi()
+    md.c_f32[1] = None                       # outputs must match across devices
+    assert call(md) == 8
+    assert call(_multi(c_layout=sp24.MULTI_SHARD), 1) == 8
+    assert call(_multi(b_layout=7)) == 8
+    md = _multi()
+    md.gemm.k = 48                           # k % 32 for 16-bit types
+    assert call(md) == 1
+    assert lib.sp24_replicate(None, 0, 16, 1, None, None, None) == 8
+    assert lib.sp24_gemm_multi_workspace_bytes(ctypes.byref(_multi(ngpu=0))) == 0
+    md = _multi()
+    md.gemm.n = 700                          # 188-column second block: B padded in workspace
+    md.b_layout = sp24.MULTI_SHARD
+    assert lib.sp24_gemm_multi_workspace_bytes(ctypes.byref(md)) == 256 * 384

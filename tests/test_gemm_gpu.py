@@ -495,7 +495,7 @@ def _layer_chain(hints, meta_format, graph, steps=6, t=16, d=2048):
         ws.append((ac, img if meta_format == sp24.META_TC else meta))
     xs = [torch.randn((d, t), device=DEV, generator=g).to(torch.bfloat16)]
     xs += [torch.empty((d, t), device=DEV, dtype=torch.bfloat16) for _ in range(steps)]
-    wsp = torch.empty(1 << 22, dtype=torch.uint8, device=DEV)
+    wsp = torch.empty(max(1 << 22, sp24.meta_tc_bytes(d, d)), dtype=torch.uint8, device=DEV)
     descs = [sp24.make_desc(ac, mt, xs[i], d, t, d, meta_format=meta_format, c_bf16=xs[i + 1],
                             workspace=wsp) for i, (ac, mt) in enumerate(ws)]
     lib = sp24.load()
@@ -525,18 +525,21 @@ def _layer_chain(hints, meta_format, graph, steps=6, t=16, d=2048):
 
 
 @pytest.mark.parametrize("graph", [False, True])
-def test_static_weight_hint_keeps_stream_order(graph):
-    """SP24_HINT_STATIC_WEIGHTS lets the narrow-N kernel load weights before
+@pytest.mark.parametrize("t,d", [(16, 2048), (64, 2048), (128, 14336)])
+def test_static_weight_hint_keeps_stream_order(graph, t, d):
+    """SP24_HINT_STATIC_WEIGHTS lets the narrow-N kernels load weights before
     the previous kernel ends; B (the previous layer's output) must still be
     read after it: a chain of layers gives bit-identical activations with and
     without the hint, eagerly and from a CUDA graph, and with reference-layout
-    metadata (repacked in-stream, so the hint is ignored)."""
-    base = _layer_chain(sp24.HINT_NONE, sp24.META_TC, graph)
-    hinted = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_TC, graph)
+    metadata (repacked in-stream, so the hint is ignored).  T = 16: the
+    split-K kernel; T = 64 over 2048 rows: the CTA-pair K-split form; T = 128
+    over 14336 rows: the narrow CTA-pair tiles."""
+    base = _layer_chain(sp24.HINT_NONE, sp24.META_TC, graph, t=t, d=d)
+    hinted = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_TC, graph, t=t, d=d)
     for a, b in zip(base, hinted):
         assert torch.isfinite(a.float()).all()
         assert torch.equal(a, b)
-    ref_fmt = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_REF, graph)
+    ref_fmt = _layer_chain(sp24.HINT_STATIC_WEIGHTS, sp24.META_REF, graph, t=t, d=d)
     for a, b in zip(base, ref_fmt):
         assert torch.equal(a, b)
 
@@ -888,6 +891,110 @@ def test_config2_bf16_8192_sampled_rows():
     lhs = (c @ ones).squeeze(1)
     rhs = (a.float() @ (b.float() @ ones)).squeeze(1)
     assert ((lhs - rhs).abs() / (rhs.abs() + 1e2)).max().item() < 1e-3
+
+
+def _pattern_2of4(m, k, gen, dist):
+    """Dense A (fp32, device) with a uniform 2:4 pattern per group of four,
+    the BASELINE configurations' generator: U(-1,1) or N(0,1) values."""
+    pat = torch.randint(0, 6, (m, k // 4), device=DEV, generator=gen)
+    if dist == "uniform":
+        vals = torch.rand((m, k // 4, 2), device=DEV, generator=gen) * 2 - 1
+    else:
+        vals = torch.randn((m, k // 4, 2), device=DEV, generator=gen)
+    vals = torch.where(vals.abs() < 1e-3, torch.full_like(vals, 0.5), vals)
+    a = torch.zeros((m, k // 4, 4), device=DEV)
+    a.scatter_(2, torch.tensor(PAIRS, device=DEV)[pat], vals)
+    return a.reshape(m, k)
+
+
+def _sampled_rows(m, seed, count=16):
+    return np.sort(np.random.default_rng(seed).choice(m, count, replace=False))
+
+
+def test_config3_e4m3_16384_sampled_rows():
+    """Benchmark configuration 3 at full size through the default dispatch:
+    e4m3 16384^3, A and B ~ N(0,1) scaled by 448/amax and rounded to e4m3 on
+    the GPU (sp24_amax_f32 + sp24_quantize_e4m3), A 2:4 with a uniform
+    pattern, bf16 out x 1/(s_A s_B).  The oracle's fp32 GEMM of the
+    dequantised values on 16 seeded rows, row-norm bound 2e-2 (the stated
+    e4m3 bound), and the compressed values / metadata of those rows against
+    the oracle's compression of the quantised A."""
+    m = n = k = 16384
+    g = torch.Generator(device=DEV).manual_seed(3)
+    af = _pattern_2of4(m, k, g, "normal")
+    bf = torch.randn((k, n), device=DEV, generator=g)
+    qa, sa = sp24.amax_quantize_e4m3(af)
+    qb, sb = sp24.amax_quantize_e4m3(bf)
+    del af, bf
+    ac_t, e_t = sp24.compress(qa)
+    alpha = 1.0 / (sa.item() * sb.item())
+    img = sp24.repack_meta(e_t, m, k, torch.uint8)
+    _, cb = sp24.gemm(ac_t, img, qb, m, n, k, meta_format=sp24.META_TC, alpha=alpha,
+                      out_f32=False, out_bf16=True, dtype=torch.uint8)
+    torch.cuda.synchronize()
+    rows = _sampled_rows(m, 3)
+    a_bits = qa[rows].cpu().numpy()
+    b_bits = qb.cpu().numpy()
+    a_c_ref, e_ref = oracle.compress(2, a_bits)
+    np.testing.assert_array_equal(e_t[rows].cpu().numpy(), e_ref)
+    np.testing.assert_array_equal(ac_t[rows].cpu().numpy(), a_c_ref)
+    a_deq = oracle.to_float(2, a_bits) / sa.item()
+    b_deq = oracle.to_float(2, b_bits) / sb.item()
+    ref = oracle.gemm(2, a_bits, b_bits, threads=os.cpu_count() or 8) * alpha
+    err = oracle.row_norm_rel_error(cb[rows].float().cpu().numpy(), ref, a_deq, b_deq)
+    assert err <= 2e-2, err
+
+
+@pytest.mark.parametrize("layer", ["up", "down"])
+@pytest.mark.parametrize("t", [64, 128, 4096])
+def test_config4_mlp_default_dispatch(layer, t):
+    """Benchmark configuration 4 at full size through the default dispatch
+    (the narrow CTA-pair tile for W_up at T = 64 / 128, the pair K-split form
+    for W_down, the 256-wide pair tiles at T = 4096): magnitude-pruned
+    N(0, 0.02) bf16 weights, activations N(0,1), bf16 out; 16 seeded rows
+    against the oracle, row-norm bound 1e-2 on the fp32 output and exact
+    rounding for the bf16 one."""
+    m, k = (14336, 4096) if layer == "up" else (4096, 14336)
+    g = torch.Generator(device=DEV).manual_seed(m + t)
+    w = (torch.randn((m, k), device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    a = sp24.prune_2of4(w)
+    b = torch.randn((k, t), device=DEV, generator=g).to(torch.bfloat16)
+    ac_t, e_t = sp24.compress(a)
+    img = sp24.repack_meta(e_t, m, k, torch.bfloat16)
+    c, cb = sp24.gemm(ac_t, img, b, m, t, k, meta_format=sp24.META_TC, out_bf16=True)
+    torch.cuda.synchronize()
+    rows = _sampled_rows(m, t)
+    a_bits, b_bits = to_host_bits(a)[rows], to_host_bits(b)
+    ref = oracle.gemm(1, a_bits, b_bits, threads=os.cpu_count() or 8)
+    err = oracle.row_norm_rel_error(c[rows].cpu().numpy(), ref, oracle.to_float(1, a_bits),
+                                    oracle.to_float(1, b_bits))
+    assert err <= 1e-2, err
+    assert torch.equal(cb, c.to(torch.bfloat16))
+
+
+def test_config5_f16_shard_sampled_rows():
+    """Benchmark configuration 5's per-GPU shard at full size: fp16 A 32768 x
+    32768 (N(0,1), uniform 2:4 pattern) times an 8192-column block of B, fp32
+    out, through the default dispatch; 16 seeded rows against the oracle
+    (row-norm bound 1e-2), compression of those rows against the oracle's."""
+    m, n, k = 32768, 8192, 32768
+    g = torch.Generator(device=DEV).manual_seed(5)
+    a = _pattern_2of4(m, k, g, "normal").to(torch.float16)
+    b = torch.randn((k, n), device=DEV, generator=g).to(torch.float16)
+    ac_t, e_t = sp24.compress(a)
+    img = sp24.repack_meta(e_t, m, k, torch.float16)
+    c, _ = sp24.gemm(ac_t, img, b, m, n, k, meta_format=sp24.META_TC)
+    torch.cuda.synchronize()
+    rows = _sampled_rows(m, 5)
+    a_bits, b_bits = to_host_bits(a[rows]), to_host_bits(b)
+    del a
+    a_c_ref, e_ref = oracle.compress(0, a_bits)
+    np.testing.assert_array_equal(e_t[rows].cpu().numpy(), e_ref)
+    np.testing.assert_array_equal(to_host_bits(ac_t[rows]), a_c_ref)
+    ref = oracle.gemm(0, a_bits, b_bits, threads=os.cpu_count() or 8)
+    err = oracle.row_norm_rel_error(c[rows].cpu().numpy(), ref, oracle.to_float(0, a_bits),
+                                    oracle.to_float(0, b_bits))
+    assert err <= 1e-2, err
 
 
 # ------------------------------------------------------------------ sharding and failure paths
