@@ -310,8 +310,9 @@ def parity_check(torch, dt, sample, b, c32, c16, alpha, k, sample_up=None):
     rank's C against an fp32 product of the same rows computed by torch on
     the device (TF32 off), as the K-scaled row-norm error
     max |C - C_ref| / (|A_r| |B_n| alpha / sqrt(K)).  With sample_up (the
-    gated SwiGLU mode) the reference is silu(A_gate B) * (A_up B) and the
-    scale the product of both GEMMs' scales.  Returns (max error, tolerance)."""
+    gated SwiGLU mode) the reference is silu(g) * u with g = A_gate B and
+    u = A_up B, and the scale each factor's K-scaled scale carried through
+    the product to first order.  Returns (max error, tolerance)."""
     a_rows, rows = sample
     prec = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -322,10 +323,14 @@ def parity_check(torch, dt, sample, b, c32, c16, alpha, k, sample_up=None):
         ref = (af @ bf) * alpha
         denom = torch.outer(af.norm(dim=1), bf.norm(dim=0)) * (alpha / k ** 0.5)
         if sample_up is not None:
+            # First-order propagation of each factor's K-scaled error through
+            # silu(g) * u:  s_g |u| + |silu(g)| s_u + s_g s_u.
             uf = f32(sample_up[0])
             up = uf @ bf
-            ref = torch.nn.functional.silu(ref) * up
-            denom = denom * torch.outer(uf.norm(dim=1), bf.norm(dim=0)) / k ** 0.5
+            s_u = torch.outer(uf.norm(dim=1), bf.norm(dim=0)) / k ** 0.5
+            sg = torch.nn.functional.silu(ref)
+            denom = denom * up.abs() + sg.abs() * s_u + denom * s_u
+            ref = sg * up
         idx = torch.from_numpy(rows).to(a_rows.device)
         got = c32[idx] if c32 is not None else c16[idx].float()
         err = ((got - ref).abs() / denom.clamp_min(1e-30)).max().item()
@@ -887,10 +892,34 @@ def main():
             a1.record(stream)
             a1.synchronize()
             lat.append(a0.elapsed_time(a1) * 1e3)
+        # The same launches captured in a CUDA graph: device time per GEMM with
+        # no host launch cost between them.
+        graph_us = None
+        try:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                cs = torch.cuda.current_stream().cuda_stream
+                for _ in range(100):
+                    step(0, cs)
+            gr.replay()
+            torch.cuda.synchronize()
+            g0 = torch.cuda.Event(enable_timing=True)
+            g1 = torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            for _ in range(5):
+                gr.replay()
+            g1.record(stream)
+            torch.cuda.synchronize()
+            graph_us = g0.elapsed_time(g1) * 1e3 / 500
+            del gr
+        except Exception as exc:   # reported in the record instead
+            graph_us = f"{type(exc).__name__}: {exc}"
         latency = {"back_to_back_us": ms_step * 1e3, "single_launch_median_us": statistics.median(lat),
                    "single_launch_min_us": min(lat), "launches": len(lat),
+                   "graph_back_to_back_us": graph_us,
                    "how": "CUDA events on the launching stream; back to back: the timed steps "
-                          "above; single: one launch between its own events, synchronised"}
+                          "above (Python launches); single: one launch between its own events, "
+                          "synchronised; graph: 100 launches captured in a CUDA graph, 5 replays"}
 
     # Gated mode: the same SwiGLU as two GEMMs plus torch's silu * mul, timed
     # the same way, for comparison.
