@@ -530,6 +530,13 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
       uint32_t soff = 0;
       bool ok = true;
       uint32_t armed_mask = 0, armed_ph = 0;
+      // 256-wide tiles: every A_c / metadata tile is read again by the pairs
+      // of the other column tiles of its raster group, several waves later;
+      // an L2 evict-last policy keeps it over B, which is reused within a
+      // wave (configurations 2 / 3 / 5: +0.5 / +1.2-2.3 / +0.4%).  Narrow
+      // tiles stream their weights once and keep the default policy.
+      const bool a_keep = BNP == 256 && !is_b;
+      const uint64_t a_pol = a_keep ? l2_evict_last_policy() : 0;
       for (int t = pair; t < P.num_tiles && ok; t += npairs) {
         int mp, nb;
         pair_tile_coords(P, t, mp, nb);
@@ -555,9 +562,13 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
             armed_mask |= 1u << s;
             armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
           }
-          if (lane < (with_e ? lanes_e : lanes_n))
-            tma_load_2d_pair(smem + soff + lane_off, lane_map,
-                             full0_leader + static_cast<uint32_t>(s * sizeof(uint64_t)), x, y);
+          if (lane < (with_e ? lanes_e : lanes_n)) {
+            const uint32_t bar = full0_leader + static_cast<uint32_t>(s * sizeof(uint64_t));
+            if (a_keep)
+              tma_load_2d_pair_hint(smem + soff + lane_off, lane_map, bar, x, y, a_pol);
+            else
+              tma_load_2d_pair(smem + soff + lane_off, lane_map, bar, x, y);
+          }
           x += dx;
           y += dy;
           soff += C::STAGE_BYTES;

@@ -308,6 +308,15 @@ SP24_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_c
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
       : "memory");
 }
+// The same load under an L2 cache policy (createpolicy).
+SP24_DEV void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                    int y, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster), "l"(pol)
+      : "memory");
+}
 SP24_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(dst_smem)),
@@ -425,6 +434,14 @@ SP24_DEV void st_global_v8(float* p, const float* v) {
 SP24_DEV uint64_t l2_evict_first_policy() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// L2 cache policy that keeps the lines it touches over others: for operand
+// tiles that other CTAs read again much later.
+SP24_DEV uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
 
