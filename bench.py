@@ -10,9 +10,17 @@ and no collective runs on the GEMM path -> weak scaling, value = total
 dense-equivalent FLOPs of all ranks / max-over-ranks time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sp24|reference]
-                    [--config 2|3|4|5] [--allgather [nccl|fused|both]]
-                    [--config 4 --layer up|down --tokens 8|16|64|128|4096]
-                    [--l2 rotate|clean]
+                    [--config 1|2|3|4|5] [--allgather [nccl|fused|both]]
+                    [--config 4 --layer up|down --tokens 8|16|64|128|4096 [--gated]]
+                    [--l2 rotate|clean] [--no-probe] [--no-strong]
+
+Every line carries `parity`: PARITY_ROWS seeded rows of every rank's C against
+an fp32 torch product of the same rows on the device (TF32 off), as the K-scaled
+row-norm error, plus bit-equality of the gathered copies when C is gathered.
+At N > 1 the line also carries `strong`: configuration 5 with its 65536 columns
+fixed in total and split over the ranks, against rank 0 running the whole
+problem alone, with the fused all-gather of C timed separately.  Configuration
+1 (one 64 x 128 x 32 tile) reports `latency` in microseconds.
 
 Configuration 4 (the MLP layers) at T <= 128 tokens is bound by HBM: its
 roofline is reported in GB/s of algorithmic bytes against the measured copy
