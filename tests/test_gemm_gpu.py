@@ -800,6 +800,16 @@ def _gated_check(m, n, k, dt, env):
     assert (np.abs(out.cpu().numpy() - ref) / bound).max() <= TOL[dt]
 
 
+@pytest.mark.parametrize("m,n,k", [(512, 96, 256), (1000, 128, 384)])
+@pytest.mark.parametrize("dt", [1, 2])
+def test_gated_silu_two_pass_short_k(m, n, k, dt):
+    """The default dispatch of a gated product with 65-128 columns, few
+    256-row tiles and a K too short to split: two passes on the plain CTA-pair
+    form, the second reading the first's value back from C in its epilogue;
+    against the composition of two plain GEMMs and against the oracle."""
+    _gated_check(m, n, k, dt, {})
+
+
 @pytest.mark.parametrize("m,n,k", [(512, 64, 2048), (768, 128, 1024), (1000, 100, 512)])
 @pytest.mark.parametrize("dt", [1, 2])
 def test_gated_silu_mlp_pair_form(m, n, k, dt):
