@@ -302,10 +302,10 @@ sp24_status sp24_ipc_close(void* base);
                     meta_format, ldb / ldc (see the layouts), alpha, tile_n.
                     Its pointer, workspace and status fields are ignored.
      b_layout       SP24_MULTI_FULL: md->b[g] is all of B (k x n, row stride
-                    ldb, 0 = n); SP24_MULTI_SHARD: md->b[g] is device g's
+                    ldb >= n, 0 = n); SP24_MULTI_SHARD: md->b[g] is device g's
                     column block alone (k x (n1 - n0), row stride n1 - n0).
      c_layout       the same for md->c_f32[g] / md->c_bf16[g] (row stride
-                    ldc, 0 = n, for FULL): a FULL C receives device g's
+                    ldc >= n, 0 = n, for FULL): a FULL C receives device g's
                     columns, and with allgather_c every device's columns.
      workspace[g]   device g's workspace (META_REF repack, B padding), at
                     least sp24_gemm_multi_workspace_bytes(md) bytes, or NULL

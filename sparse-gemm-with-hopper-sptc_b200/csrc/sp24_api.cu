@@ -1227,6 +1227,12 @@ sp24_status validate_multi(const sp24_multi_desc* md, int allgather_c) {
       return SP24_ERR_ARG;
   }
   if (md->gemm.m <= 0 || md->gemm.n <= 0 || md->gemm.k <= 0) return SP24_ERR_SHAPE;
+  // Whole-matrix layouts address a device's columns through the row stride,
+  // which must then span all n columns (a shard's own check sees only its width).
+  if (md->b_layout == SP24_MULTI_FULL && md->gemm.ldb != 0 && md->gemm.ldb < md->gemm.n)
+    return SP24_ERR_SHAPE;
+  if (md->c_layout == SP24_MULTI_FULL && md->gemm.ldc != 0 && md->gemm.ldc < md->gemm.n)
+    return SP24_ERR_SHAPE;
   return SP24_OK;
 }
 

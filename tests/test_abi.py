@@ -153,6 +153,15 @@ def test_gemm_multi_rejects_bad_descriptors_before_any_launch():
     md = _multi()
     md.gemm.k = 48                           # k % 32 for 16-bit types
     assert call(md) == 1
+    md = _multi()
+    md.gemm.ldc = 300                        # a whole-matrix C must span all 512 columns
+    assert call(md) == 1
+    md = _multi()
+    md.gemm.ldb = 300
+    assert call(md) == 1
+    md = _multi(b_layout=sp24.MULTI_SHARD, c_layout=sp24.MULTI_SHARD)
+    md.gemm.ldc = md.gemm.ldb = 300          # column-block layouts use their own widths
+    assert lib.sp24_gemm_multi_workspace_bytes(ctypes.byref(md)) == 0
     assert lib.sp24_replicate(None, 0, 16, 1, None, None, None) == 8
     assert lib.sp24_gemm_multi_workspace_bytes(ctypes.byref(_multi(ngpu=0))) == 0
     md = _multi()
