@@ -412,6 +412,15 @@ SP24_DEV void pair_store_row_to(const PairParams& P, float* c32, __nv_bfloat16* 
   }
 }
 
+// Bytes both CTAs of a pair load for stage ks of a tile (counted on the
+// leader's full barrier): every stage carries A_c and B, and the metadata
+// atoms come with the first stage of each SPA group.
+template <typename C>
+SP24_DEV uint32_t pair_stage_tx(int ks) {
+  const bool with_e = (C::SPA == 1) || (ks % C::SPA) == 0;
+  return 2u * static_cast<uint32_t>(C::STAGE_BYTES - (with_e ? 0 : C::E_BYTES));
+}
+
 // The kernel body.  KS = 0: clusters of 2, persistent over the tiles.
 // KS = 1 (K-split form, for too few 256-row tiles to occupy the GPU): a
 // cluster of 2 S CTAs computes one tile; pair p (CTAs 2p, 2p+1) accumulates
@@ -454,21 +463,21 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
   if (threadIdx.x == 0) {
     abort_sh = 0;
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full_bar[s], C::SPA == 1 ? 1 : 2);  // fine stages: one arming per producer warp
+      mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&accf_bar, 1);
     mbar_init(&acce_bar, 2 * kPairEpiWarps);
     mbar_init(&drain_bar, 1);
     fence_barrier_init();
-    // Coarse stages all carry the same bytes, so the leader arms every full
-    // barrier for its first use here and the MMA warp re-arms a slot for its
-    // next use as soon as it has seen the slot's data arrive: the producers'
-    // per-stage work shrinks to one slot wait and one TMA issue.
-    if constexpr (C::SPA == 1) {
-      if (leader)
-        for (int s = 0; s < C::STAGES; ++s) mbar_arrive_expect_tx(&full_bar[s], 2u * C::STAGE_BYTES);
-    }
+    // The leader arms every full barrier for its first use here and the MMA
+    // warp re-arms a slot for its next use as soon as it has seen the slot's
+    // data arrive: the producers' per-stage work shrinks to one slot wait and
+    // one TMA issue.  Coarse stages all carry the same bytes; fine stages
+    // carry a metadata atom every SPA-th stage of a tile (pair_stage_tx).
+    if (leader)
+      for (int s = 0; s < C::STAGES; ++s)
+        mbar_arrive_expect_tx(&full_bar[s], pair_stage_tx<C>(s % max(1, kst1 - kst0) + kst0));
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -521,8 +530,6 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
                        : static_cast<uint32_t>(C::A_BYTES + C::B_BYTES + el * kAtomBytes));
       const int lanes_e = is_b ? C::B_BOXES : G + G * C::E_PER;  // stages that carry metadata
       const int lanes_n = is_b ? C::B_BOXES : G;                 // stages that do not
-      const uint32_t tx_e = 2u * (is_b ? C::B_BYTES : C::A_BYTES + C::E_BYTES);
-      const uint32_t tx_n = 2u * (is_b ? C::B_BYTES : C::A_BYTES);
       const int dx = is_a ? C::A_COLS : 0;
       const int dy = is_b ? C::BKD : (is_a ? 0 : C::E_PER * P.m_blocks * 8 / C::SPA);
       int s = 0;
@@ -554,10 +561,6 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
             break;
           }
           const bool with_e = (C::SPA == 1) || (ks % C::SPA) == 0;
-          if constexpr (C::SPA != 1) {
-            if (leader && lane == 0) mbar_arrive_expect_tx(&full_bar[s], with_e ? tx_e : tx_n);
-            __syncwarp();
-          }
           if (leader && lane == 0) {
             armed_mask |= 1u << s;
             armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
@@ -626,8 +629,13 @@ SP24_DEV void pair_gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB,
             ok = false;
             break;
           }
-          if constexpr (C::SPA == 1) {
-            if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], 2u * C::STAGE_BYTES);
+          if (lane == 0) {
+            // Re-arm the slot for the stage STAGES later in this pair's
+            // sequence (it may fall in a later tile, or after the last one,
+            // where the arming is never consumed).
+            int nks = ks + C::STAGES;
+            while (nks >= kst1) nks -= max(1, kst1 - kst0);
+            mbar_arrive_expect_tx(&full_bar[s], pair_stage_tx<C>(nks));
           }
           tc_fence_after();
           const int sub = ks % C::SPA;

@@ -229,6 +229,33 @@ def test_alpha_and_strided_output(dt):
     assert (big[:, n:] == -1.0).all()
 
 
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k", [(512, 512, 192), (300, 700, 448), (768, 1024, 2048)])
+def test_pair_fine_stages(dt, m, n, k):
+    """The CTA-pair kernel's fine stages (SP24_PAIR_FINE=1: half-size stages;
+    for 16-bit types one metadata atom per two stages, so a tile with an odd
+    stage count moves the atom pattern across tiles in the ring): against
+    the coarse stages, which issue the same MMAs in the same K order (bit for
+    bit), and against the oracle."""
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    gen = oracle.Gen(m + n + k + dt)
+    a, b, _, _, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    img = sp24.repack_meta(e_t, m, k, lib_dtype(dt))
+    b_t = to_dev(b, dt)
+
+    def run():
+        c, _ = sp24.gemm(ac_t, img, b_t, m, n, k, meta_format=sp24.META_TC, dtype=lib_dtype(dt))
+        return c
+
+    fine = _with_env({"SP24_KERNEL": "2sm", "SP24_PAIR_FINE": "1"}, run)
+    coarse = _with_env({"SP24_KERNEL": "2sm"}, run)
+    torch.cuda.synchronize()
+    assert torch.equal(fine, coarse)
+    check_c(fine, c_ref, a, b, dt, abs_rule=False)
+
+
 def test_kernels_agree():
     """The single-CTA and CTA-pair kernels run the same K order per output."""
     gen = oracle.Gen(8)
