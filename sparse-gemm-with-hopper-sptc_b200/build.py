@@ -13,6 +13,9 @@
   build_probe()    lib/libsp24_peak.so — the tensor-core rate probe that bench.py
                    and the tests use to measure the roofline's peak (measurement
                    infrastructure, not part of the C ABI).
+  build_feed_probe() bin/sp24_feed_probe — the shared-memory feed probe: TMA
+                   ring fill rates with a slot-holding consumer, from L2 and
+                   from HBM (measurement only; run by hand).
   build_oracle()   oracle/lib + oracle/_ref (test infrastructure, see oracle/).
 
 ``python sparse-gemm-with-hopper-sptc_b200/build.py [--force]`` builds all.
@@ -74,6 +77,15 @@ def build_probe(force: bool = False) -> str:
 
 DROPIN = os.path.join(HERE, "dropin")
 BINDIR = os.path.join(HERE, "bin")
+
+
+def build_feed_probe(force: bool = False) -> str:
+    os.makedirs(BINDIR, exist_ok=True)
+    out = os.path.join(BINDIR, "sp24_feed_probe")
+    src = os.path.join(CSRC, "sp24_feed_probe.cu")
+    if force or _stale(out, [src, os.path.join(CSRC, "sp24_ptx.cuh")]):
+        _run([NVCC, *ARCH, "-O3", "-std=c++17", "-lineinfo", src, "-o", out])
+    return out
 # The reference checkout: SP24_REF_DIR, else a `reference` directory beside
 # the repository.  Only the drop-in and oracle builds read it, and only when
 # it exists.
@@ -160,6 +172,7 @@ def build_oracle(ref_dir: str = REF_DIR) -> None:
 def build_all(force: bool = False) -> None:
     build_lib(force=force)
     build_probe(force=force)
+    build_feed_probe(force=force)
     build_oracle()
     build_dropin(force=force)
     build_raw_kernel_check(force=force)
