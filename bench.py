@@ -187,7 +187,14 @@ def job_gpus(world):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    polled from a thread every ~1 ms (a 20-step configuration-2 region lasts
+    ~10 ms), with nvidia-smi (50 ms) as the fallback when NVML is missing."""
+
+    # NVML clocks-event reason bits (nvml.h: SwPowerCap, HwSlowdown,
+    # SwThermalSlowdown, HwThermalSlowdown)
+    NVML_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+                    0x40: "hw_thermal_slowdown"}
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -195,7 +202,11 @@ class ClockSampler:
 
     def __init__(self, gpus):
         self.gpus = ",".join(str(g) for g in gpus)
+        self.gpu_ids = [str(g) for g in gpus]
         self.proc = None
+        self.nvml = []          # (sm_mhz, max_mhz, reason bits) per sample and GPU
+        self._stop = None
+        self._thread = None
         # Raw samples go to a scratch file (SP24_CLOCKS_DIR, else the system's
         # temporary directory); the JSON line carries their summary.
         out_dir = os.environ.get("SP24_CLOCKS_DIR", tempfile.gettempdir())
@@ -225,9 +236,44 @@ class ClockSampler:
                 self.skip = sum(1 for _ in fh)   # samples taken before the region
         except OSError:
             pass
+        self._start_nvml()
         return self
 
+    def _start_nvml(self):
+        try:
+            import threading
+            import pynvml
+            pynvml.nvmlInit()
+            handles = []
+            for g in self.gpu_ids:
+                if g.isdigit():
+                    handles.append(pynvml.nvmlDeviceGetHandleByIndex(int(g)))
+                else:
+                    handles.append(pynvml.nvmlDeviceGetHandleByUUID(g))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            maxes = [pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in handles]
+        except Exception:   # NVML missing or refused: nvidia-smi samples only
+            return
+        self._stop = threading.Event()
+
+        def poll():
+            while not self._stop.is_set():
+                for h, mx in zip(handles, maxes):
+                    try:
+                        self.nvml.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                          mx, int(get_reasons(h))))
+                    except Exception:
+                        pass
+                time.sleep(0.001)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
+
     def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(2.0)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -237,6 +283,15 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
+        if self.nvml:
+            reasons = set()
+            for _, _, bits in self.nvml:
+                for bit, nm in self.NVML_REASONS.items():
+                    if bits & bit:
+                        reasons.add(nm)
+            return {"sm_mhz": statistics.median(x[0] for x in self.nvml),
+                    "sm_max_mhz": max(x[1] for x in self.nvml), "reasons": sorted(reasons),
+                    "samples": len(self.nvml), "source": "NVML, ~1 ms polling"}
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
