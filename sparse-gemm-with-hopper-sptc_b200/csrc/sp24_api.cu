@@ -21,6 +21,7 @@
 #include "sp24_gemm_kernel.cuh"
 #include "sp24_gemm_splitk_kernel.cuh"
 #include "sp24_prep.cuh"
+#include "../dropin/sp24_raw_kernel.cuh"
 
 namespace {
 
@@ -176,6 +177,8 @@ struct Tuning {
   int splitk_kb = 0;          // SP24_SPLITK_KB=1|2 (0 = chosen per tile width)
   int gated = 0;              // SP24_GATED=1|2: gated SwiGLU form forced
   int pair_gated = 1;         // SP24_PAIR_GATED set: gated CTA-pair form off
+  int raw_route = 1;          // SP24_RAW_ROUTE=0: tiny reference-layout problems take the
+                              //   repack + dispatch path too
 };
 
 Tuning read_tuning() {
@@ -207,6 +210,7 @@ Tuning read_tuning() {
   if (num("SP24_SPLITK_KB", &v) && (v == 1 || v == 2)) t.splitk_kb = v;
   if (num("SP24_GATED", &v)) t.gated = v;
   if (std::getenv("SP24_PAIR_GATED") != nullptr) t.pair_gated = 0;
+  if (num("SP24_RAW_ROUTE", &v)) t.raw_route = v != 0;
   return t;
 }
 
@@ -903,6 +907,67 @@ sp24_status validate_peers(const sp24_gemm_desc* d, const sp24_peer_out* peers) 
   return SP24_OK;
 }
 
+// Size limits of the tiny reference-layout route.  Measured on B200, back to
+// back from the host, bf16: 64x128x32 6.2 against 9.9 us, 64x256x64 8.2
+// against 16.4 us, 128x256x128 9.8 against 16.4 us; 256x256x256 ties (12.3
+// us), and from K = 512 on the route loses (256x256x512 18.3 against 12.3).
+constexpr int kRawRouteMaxM = 256;
+constexpr int kRawRouteMaxN = 256;
+constexpr int kRawRouteMaxK = 256;
+constexpr long long kRawRouteMaxMNK = 128LL * 256 * 256;
+
+// Tiny problems in the reference's own metadata layout: one launch of the
+// launchable M = 64 kernel (dropin/sp24_raw_kernel.cuh), which reads the
+// reference's nibbles inside the kernel, instead of a repack launch followed
+// by the CTA-pair kernel, whose setup would be most of the time.  The route
+// takes exactly what that kernel takes: fp16 / bf16 / e4m3, fp32 output only,
+// alpha 1, packed rows (A_c k / 2, B and C n), M % 64 == 0, K % 32 (e4m3:
+// % 64), 16-byte aligned operands, no fused epilogue and no peers.  Returns
+// the tile width to launch, 0 when the problem does not take the route.
+int raw_route_bn(const sp24_gemm_desc* d, const sp24_epilogue* e, const sp24_peer_out* peers,
+                 const Tuning& t) {
+  if (!t.raw_route || t.kernel_set || e != nullptr || peers != nullptr) return 0;
+  if (d->meta_format != SP24_META_REF) return 0;
+  if (d->dtype != SP24_F16 && d->dtype != SP24_BF16 && d->dtype != SP24_E4M3) return 0;
+  if (d->c_f32 == nullptr || d->c_bf16 != nullptr) return 0;
+  if (d->alpha != 0.0f && d->alpha != 1.0f) return 0;
+  if (d->m % 64 != 0 || d->m > kRawRouteMaxM || d->n > kRawRouteMaxN || d->k > kRawRouteMaxK ||
+      static_cast<long long>(d->m) * d->n * d->k > kRawRouteMaxMNK)
+    return 0;
+  if (d->k % (d->dtype == SP24_E4M3 ? 64 : 32) != 0) return 0;
+  if ((d->lda_c != 0 && d->lda_c != d->k / 2) || (d->ldb != 0 && d->ldb != d->n) ||
+      (d->ldc != 0 && d->ldc != d->n))
+    return 0;
+  if (!aligned16(d->a_c) || !aligned16(d->b) || !aligned16(d->meta) || !aligned16(d->c_f32))
+    return 0;
+  for (int bn = 256; bn >= 8; bn >>= 1)
+    if (d->n % bn == 0 && (d->tile_n == 0 || bn <= d->tile_n)) return bn;
+  return 0;
+}
+
+template <typename T>
+sp24_status launch_raw_t(const sp24_gemm_desc* d, int bn, cudaStream_t stream) {
+  const T* a = static_cast<const T*>(d->a_c);
+  const T* b = static_cast<const T*>(d->b);
+  const dim3 grid(static_cast<unsigned>(d->n / bn), static_cast<unsigned>(d->m / 64));
+  switch (bn) {
+    case 256: wgmma_sp_raw_kernel<T, 256><<<grid, 128, 0, stream>>>(a, b, d->meta, d->c_f32, d->n, d->k); break;
+    case 128: wgmma_sp_raw_kernel<T, 128><<<grid, 128, 0, stream>>>(a, b, d->meta, d->c_f32, d->n, d->k); break;
+    case 64: wgmma_sp_raw_kernel<T, 64><<<grid, 128, 0, stream>>>(a, b, d->meta, d->c_f32, d->n, d->k); break;
+    case 32: wgmma_sp_raw_kernel<T, 32><<<grid, 128, 0, stream>>>(a, b, d->meta, d->c_f32, d->n, d->k); break;
+    case 16: wgmma_sp_raw_kernel<T, 16><<<grid, 128, 0, stream>>>(a, b, d->meta, d->c_f32, d->n, d->k); break;
+    default: wgmma_sp_raw_kernel<T, 8><<<grid, 128, 0, stream>>>(a, b, d->meta, d->c_f32, d->n, d->k); break;
+  }
+  SP24_CUDA_TRY(cudaGetLastError());
+  return SP24_OK;
+}
+
+sp24_status launch_raw(const sp24_gemm_desc* d, int bn, cudaStream_t stream) {
+  if (d->dtype == SP24_F16) return launch_raw_t<half>(d, bn, stream);
+  if (d->dtype == SP24_BF16) return launch_raw_t<__nv_bfloat16>(d, bn, stream);
+  return launch_raw_t<__nv_fp8_e4m3>(d, bn, stream);
+}
+
 sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned long long timeout_ns,
                       int stall, const sp24_epilogue* e = nullptr,
                       const sp24_peer_out* peers = nullptr) {
@@ -958,6 +1023,7 @@ sp24_status gemm_impl(const sp24_gemm_desc* d, cudaStream_t stream, unsigned lon
       (g_launch_hints & SP24_HINT_STATIC_WEIGHTS) != 0 && d->meta_format == SP24_META_TC ? 1 : 0;
   p.tune = tuning();
 
+  if (const int rbn = raw_route_bn(d, e, peers, p.tune)) return launch_raw(d, rbn, stream);
   if (d->meta_format == SP24_META_REF) {
     st = sp24_repack_meta(d->dtype, d->meta, d->m, d->k, ws + w.meta_off,
                           reinterpret_cast<sp24_stream_t>(stream));
@@ -1453,11 +1519,18 @@ sp24_status sp24_last_kernel_status(sp24_stream_t stream) {
   sp24_status st = device_info(&di);
   if (st != SP24_OK) return st;
   cudaStream_t s = as_stream(stream);
-  int h = 0;
+  int h = 0, hr = 0;
   SP24_CUDA_TRY(cudaMemcpyAsync(&h, di->status_word, sizeof(int), cudaMemcpyDeviceToHost, s));
+  // The tiny reference-layout route's kernel keeps its own flag.
+  SP24_CUDA_TRY(cudaMemcpyFromSymbolAsync(&hr, sp24_raw_kernel_status, sizeof(int), 0,
+                                          cudaMemcpyDeviceToHost, s));
   SP24_CUDA_TRY(cudaStreamSynchronize(s));
-  if (h) {
-    SP24_CUDA_TRY(cudaMemsetAsync(di->status_word, 0, sizeof(int), s));
+  if (h || hr) {
+    const int zero = 0;
+    if (h) SP24_CUDA_TRY(cudaMemsetAsync(di->status_word, 0, sizeof(int), s));
+    if (hr)
+      SP24_CUDA_TRY(cudaMemcpyToSymbolAsync(sp24_raw_kernel_status, &zero, sizeof(int), 0,
+                                            cudaMemcpyHostToDevice, s));
     SP24_CUDA_TRY(cudaStreamSynchronize(s));
     return SP24_ERR_TIMEOUT;
   }

@@ -364,6 +364,39 @@ def test_pair_splitk_matches_oracle(dt, m, n, k, splits):
     assert (c - c_one).abs().max().item() <= 1e-5 * scale
 
 
+@pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("m,n,k", [(64, 128, 32), (128, 256, 128), (256, 128, 64), (64, 8, 64),
+                                   (192, 48, 256)])
+def test_raw_route_matches_dispatch(dt, m, n, k):
+    """Tiny problems in the reference's metadata layout run as one launch of
+    the M = 64 launchable kernel (SP24_RAW_ROUTE, on by default): against the
+    oracle, and within fp32 rounding of the repack + dispatch path that
+    SP24_RAW_ROUTE=0 keeps.  Problems the route does not take (bf16 output
+    requested) still go the other way and stay correct."""
+    if dt == 2 and k % 64:
+        pytest.skip("e4m3 needs k % 64")
+    gen = oracle.Gen(11 * m + 3 * n + k + dt)
+    a, b, _, _, c_ref = oracle.host_case(gen, dt, m, n, k, False)
+    ac_t, e_t = sp24.compress(to_dev(a, dt))
+    b_t = to_dev(b, dt)
+
+    def run(out_bf16=False):
+        return sp24.gemm(ac_t, e_t, b_t, m, n, k, out_bf16=out_bf16, dtype=lib_dtype(dt))
+
+    routed, _ = _with_env({"SP24_RAW_ROUTE": "1"}, run)
+    routed2, _ = _with_env({"SP24_RAW_ROUTE": "1"}, run)
+    plain, _ = _with_env({"SP24_RAW_ROUTE": "0"}, run)
+    both, both16 = _with_env({"SP24_RAW_ROUTE": "1"}, lambda: run(True))
+    torch.cuda.synchronize()
+    assert sp24.last_kernel_status() == 0
+    check_c(routed, c_ref, a, b, dt, abs_rule=(dt != 2))
+    check_c(both, c_ref, a, b, dt, abs_rule=(dt != 2))
+    assert torch.equal(routed, routed2)
+    assert torch.equal(both16, both.to(torch.bfloat16))
+    scale = plain.abs().max().item() + 1.0
+    assert (routed - plain).abs().max().item() <= 1e-5 * scale
+
+
 def test_pair_splitk_epilogue():
     """alpha, per-row bias and SiLU applied once, after the slices are summed."""
     m, n, k = 640, 128, 4096
