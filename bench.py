@@ -261,19 +261,29 @@ class ClockSampler:
             while not self._stop.is_set():
                 for h, mx in zip(handles, maxes):
                     try:
-                        self.nvml.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                        self._raw.append((time.perf_counter(),
+                                          pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
                                           mx, int(get_reasons(h))))
                     except Exception:
                         pass
-                time.sleep(0.001)
+                time.sleep(0.0002)
 
+        self._raw = []
         self._thread = threading.Thread(target=poll, daemon=True)
         self._thread.start()
+        # The timed region starts once the poller is running; only samples
+        # taken between here and __exit__ count.
+        t0 = time.perf_counter()
+        while not self._raw and time.perf_counter() - t0 < 1.0:
+            time.sleep(0.0005)
+        self._t_begin = time.perf_counter()
 
     def __exit__(self, *exc):
         if self._thread is not None:
+            t_end = time.perf_counter()
             self._stop.set()
             self._thread.join(2.0)
+            self.nvml = [x[1:] for x in self._raw if self._t_begin <= x[0] <= t_end]
         if self.proc is not None:
             self.proc.terminate()
             try:
